@@ -1,0 +1,459 @@
+"""Benchmark of the HilbertA paired block-sparse attention on B200.
+
+Metric: ms/call + effective TFLOP/s over ACTIVE 64x64 blocks of
+the sparse attention at 2048^2 (128x128 image grid + 512 text tokens = 16896
+tokens), 16 tiles, bridge K=3, B=1, 24 heads x 128, bf16 Q/K/V ~ N(0,1) from
+torch seed 2707 (the reference benchmark's protocol, hilberta/benchmark.py:24-85).
+
+One step = one attention call for each of the four tile phases (phases 0..3 of
+the plan); ms/call is phase-weighted 15/14/14/14 over 57 layers
+(benchmark.py:76-83).  FLOP per call = H * 4*64*64*D * A, A = active 64x64
+(query-block, key-block) pairs (global rows x all blocks + sum of kv_counts).
+
+N > 1 (torchrun): head-parallel, rank r owns heads [r*H/P, (r+1)*H/P); a step
+adds the NCCL all-gather of the bf16 head outputs (what the FLUX block consumes);
+``value`` = total active FLOP of all ranks / max-over-ranks device time.
+
+``--impl reference`` times the reference's dense-mask CPU path (plan mask +
+fp32 SDPA, the computation of hilberta/flux_adapter.py:299-307) restated in
+oracle/attention_oracle.py, on a bounded row sample, with all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+CONFIGS = {
+    # name: (resolution, tiles, k)
+    "1024_t4k1": (1024, 4, 1),
+    "1024_t16k3": (1024, 16, 3),
+    "2048_t4k1": (2048, 4, 1),
+    "2048_t16k3": (2048, 16, 3),
+    "4096_t16k3": (4096, 16, 3),
+}
+WEIGHTS = (15, 14, 14, 14)
+METRIC = "ms/call + effective TFLOP/s (active blocks) of sparse attn, 2048² t16k3, 1/2/4/8 B200"
+FALLBACK_PEAK_TFLOPS = 1590.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="2048_t16k3")
+    ap.add_argument("--heads", type=int, default=24)
+    ap.add_argument("--layout", choices=["bhnd", "bnhd"], default="bhnd")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU seconds of the baseline sample")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    return FALLBACK_PEAK_TFLOPS, FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(config):
+    """Per-launch DRAM bytes of k_paired_fwd from the committed ncu summary, if any."""
+    f = ROOT / "profiles" / f"paired_fwd_{config}_traffic.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch="):
+            return float(line.split("=", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except (OSError, ValueError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.result = None
+        if self.proc is None:
+            return False
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        mhz, maxmhz, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                idx = int(f[0])
+            except ValueError:
+                continue
+            if idx not in self.gpus:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                maxmhz = max(maxmhz, float(f[2]))
+            except ValueError:
+                pass
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if mhz:
+            self.result = {"sm_mhz": statistics.median(mhz), "sm_max_mhz": maxmhz, "reasons": sorted(reasons),
+                           "samples": len(mhz)}
+        return False
+
+
+def build_workload(config, heads, layout, device, head_slice=None):
+    import hilberta_b200 as hb
+
+    res, tiles, k = CONFIGS[config]
+    plan = hb.bridge_k_plan(tiles, k, False, grid_size=res // 16, device=device)
+    N, G = plan.total_tokens, plan.global_tokens
+    metas, active = [], []
+    for p in plan.phases:
+        metas.append(hb.pair_metadata(p.kv_indices, p.kv_counts, tokens=N, global_tokens=G).to(device))
+        active.append((G // 64) * (N // 64) + int(p.kv_counts.sum()))
+    g = torch.Generator(device="cpu").manual_seed(2707)
+    shape = (1, heads, N, 128) if layout == "bhnd" else (1, N, heads, 128)
+    qkv = [torch.randn(shape, generator=g, dtype=torch.float32).to(torch.bfloat16) for _ in range(3)]
+    if layout == "bnhd":
+        qkv = [x.transpose(1, 2) for x in qkv]
+    if head_slice is not None:
+        qkv = [x[:, head_slice] for x in qkv]
+    return plan, metas, active, qkv
+
+
+def flop_per_call(active, heads, D=128):
+    return heads * 4 * 64 * 64 * D * active
+
+
+def run_native(a):
+    import torch.distributed as dist
+
+    import hilberta_b200 as hb
+
+    rank, world, local = dist_env()
+    if world != a.gpus:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    H = a.heads
+    if H % world:
+        raise SystemExit("heads must divide across ranks")
+    hr = H // world
+    hs = slice(rank * hr, (rank + 1) * hr)
+    plan, metas, active, qkv_host = build_workload(a.config, H, a.layout, dev, head_slice=hs)
+    N = plan.total_tokens
+    q, k, v = (x.to(dev) for x in qkv_host)
+    out = torch.empty_like(q)
+    gathered = torch.empty(world, 1, hr, N, 128, dtype=torch.bfloat16, device=dev) if world > 1 else None
+    stream = torch.cuda.current_stream(dev)
+
+    def call(ph):
+        hb.paired_attention(q, k, v, metas[ph], global_strategy="triton", num_warps=8, num_stages=2, out=out)
+
+    def gather():
+        if world > 1:
+            dist.all_gather_into_tensor(gathered.view(-1), out.contiguous().view(-1))
+
+    with torch.inference_mode():
+        for _ in range(max(3, a.warmup)):
+            for ph in range(4):
+                call(ph)
+                gather()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(4)]
+              for _ in range(a.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler([local] if world == 1 else range(world)) as clk:
+            torch.cuda.synchronize()
+            t0.record(stream)
+            for s in range(a.steps):
+                for ph in range(4):
+                    ev[s][ph][0].record(stream)
+                    call(ph)
+                    ev[s][ph][1].record(stream)
+                    gather()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+        status = hb.device_status(dev)
+    total_ms = t0.elapsed_time(t1)
+    per_phase = [[ev[s][ph][0].elapsed_time(ev[s][ph][1]) for s in range(a.steps)] for ph in range(4)]
+    kern_ms = [statistics.mean(x) for x in per_phase]
+    t = torch.tensor([total_ms, *kern_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, kern_ms = float(t[0]), [float(x) for x in t[1:]]
+    flops = [flop_per_call(A, H) for A in active]  # whole job (all heads)
+    weighted_ms = sum(w * m for w, m in zip(WEIGHTS, kern_ms)) / 57
+    weighted_flop = sum(w * f for w, f in zip(WEIGHTS, flops)) / 57
+    value = sum(flops) * a.steps / (total_ms * 1e-3) / 1e12
+
+    e2e = None
+    if not a.no_e2e:
+        e2e = run_e2e(a, q, k, v, metas, flops, world, dev, hb)
+    peak, hbm, peak_kind = peaks()
+    achieved = weighted_flop / world / (weighted_ms * 1e-3) / 1e12  # one GPU's launch
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(a, plan, active, bounded=a.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        del gathered
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    traffic = ncu_traffic(a.config)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": max(3, a.warmup),
+        "ms_per_step": round(total_ms / a.steps, 4),
+        "ms_per_call": round(weighted_ms, 4),
+        "ms_per_call_by_phase": [round(x, 4) for x in kern_ms],
+        "eff_tflops_kernel": round(weighted_flop / (weighted_ms * 1e-3) / 1e12, 2),
+        "frac_peak": round(achieved / peak, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 Q/K/V, reference benchmark protocol)",
+        "config": {
+            "workload": f"HilbertA paired sparse attention {a.config}, B=1, H={H}, D=128, N={N}, G=512",
+            "layout": a.layout,
+            "heads_per_gpu": hr,
+            "step": "4 calls (tile phases 0-3)" + (" each + NCCL all-gather of head outputs" if world > 1 else ""),
+            "parallelism": f"head-parallel x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (Q+K+V %.0f MB)" % (3 * N * H * 128 * 2 / 1e6),
+            "active_blocks_per_phase": active,
+        },
+        "gpu_launches": 4 * a.steps,
+        "device_status": status,
+        "roofline": {
+            "bound": "tensor",
+            "achieved": round(achieved, 2),
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4),
+            "peak_source": f"{peak_kind} bf16 dense (MEASURED_PEAKS.json bf16_tflops, burst)" if peak_kind == "measured" else "fallback 1.59 PFLOP/s",
+            "traffic": traffic,
+            "kernel": "k_paired_fwd",
+        },
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if clk.result is not None:
+        line["clocks"] = clk.result
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(a, q, k, v, metas, flops, world, dev, hb):
+    """Same metric through the public call with HOST buffers: per call, pinned
+    Q/K/V host->device, paired_attention, output device->host."""
+    import torch.distributed as dist
+
+    hq, hk, hv = (x.detach().cpu().contiguous().pin_memory() for x in (q, k, v))
+    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    dq, dk, dv = (torch.empty_like(x, device=dev) for x in (hq, hk, hv))
+    dout = torch.empty_like(dq)
+    steps = max(1, min(a.steps, 5))
+
+    def one(ph):
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        hb.paired_attention(dq, dk, dv, metas[ph], global_strategy="triton", num_warps=8, num_stages=2, out=dout)
+        hout.copy_(dout, non_blocking=True)
+
+    with torch.inference_mode():
+        for ph in range(4):
+            one(ph)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            for ph in range(4):
+                one(ph)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms[0])
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv)) * 4 * world
+    d2h = hout.numel() * hout.element_size() * 4 * world
+    return {
+        "value": round(sum(flops) * steps / (ms * 1e-3) / 1e12, 3),
+        "unit": "TFLOP/s",
+        "ms_per_step": round(ms / steps, 3),
+        "h2d_bytes_per_step": h2d,
+        "d2h_bytes_per_step": d2h,
+        "steps": steps,
+        "note": "per call: pinned Q/K/V H2D + paired_attention + O D2H, through hilberta_b200.paired_attention",
+    }
+
+
+def cpu_baseline(a, plan, active, bounded=15.0):
+    """Reference dense-mask CPU path (oracle port) on a bounded row sample."""
+    import numpy as np
+
+    from oracle import attention_oracle as ao
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    H = a.heads
+    N, G = plan.total_tokens, plan.global_tokens
+    p = plan.phases[0]
+    bm = ao.block_mask_from_rows(p.kv_indices.numpy(), p.kv_counts.numpy(), N, G)
+    row_active = bm.sum(1).repeat(64)  # active key blocks per query row
+    g = torch.Generator().manual_seed(2707)
+    q, k, v = (torch.randn(1, H, N, 128, generator=g).to(torch.bfloat16) for _ in range(3))
+    rng = np.random.default_rng(0)
+    # probe with a small sample, then size the sample to ~`bounded` seconds
+    rows = np.sort(rng.choice(N, 16, replace=False))
+    t = time.perf_counter()
+    ao.masked_attention_fp32(q, k, v, bm, rows=rows, chunk=256)
+    per_row = (time.perf_counter() - t) / len(rows)
+    n = int(max(16, min(N, bounded / max(per_row, 1e-6))))
+    rows = np.sort(rng.choice(N, n, replace=False))
+    t = time.perf_counter()
+    ao.masked_attention_fp32(q, k, v, bm, rows=rows, chunk=256)
+    sec = time.perf_counter() - t
+    sampled_flop = H * 4 * 64 * 128 * float(row_active[rows].sum())
+    tflops = sampled_flop / sec / 1e12
+    full_call_s = sec * (flop_per_call(active[0], H) / sampled_flop)
+    return {
+        "value": round(tflops, 5),
+        "unit": "TFLOP/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{n} of {N} query rows x {H} heads, phase 0, dense-mask fp32 SDPA (torch CPU); "
+        f"{sec:.1f} s; extrapolated {full_call_s:.1f} s per call",
+        "ms_per_call_extrapolated": round(full_call_s * 1e3, 1),
+    }
+
+
+def run_reference(a):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import hilberta_b200  # noqa: F401  (plan built on the GPU when one is present)
+
+    res, tiles, k = CONFIGS[a.config]
+    if torch.cuda.is_available():
+        from hilberta_b200 import bridge_k_plan
+
+        plan = bridge_k_plan(tiles, k, False, grid_size=res // 16)
+    else:
+        from oracle import plan_oracle as po
+
+        plan = po.bridge_k_plan(tiles, k, False, grid_size=res // 16)
+    N, G = plan.total_tokens, plan.global_tokens
+    active = [(G // 64) * (N // 64) + int(p.kv_counts.sum()) for p in plan.phases]
+    steps = max(1, a.steps)
+    per_step = max(2.0, 60.0 / (steps + max(3, a.warmup)))
+    vals = []
+    cpu = None
+    for i in range(max(1, min(a.warmup, 1)) + steps):
+        cpu = cpu_baseline(a, plan, active, bounded=per_step)
+        if i >= 1:
+            vals.append(cpu["value"])
+    value = statistics.median(vals)
+    ms_call = flop_per_call(sum(w * x for w, x in zip(WEIGHTS, active)) / 57, a.heads) / (value * 1e12) * 1e3
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "impl": "reference",
+        "n_gpus": a.gpus,
+        "steps": steps,
+        "warmup": 1,
+        "ms_per_step": round(ms_call * 4, 1),
+        "ms_per_call": round(ms_call, 1),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32 (from bf16 inputs)",
+        "data": "synthetic (seeded N(0,1) bf16 Q/K/V)",
+        "config": {"workload": f"HilbertA sparse attention {a.config}, B=1, H={a.heads}, D=128, N={N}, G=512",
+                   "path": "reference dense-mask CPU path restated (plan.dense_mask + fp32 SDPA), row-sampled"},
+        "cpu_baseline": {k2: cpu[k2] for k2 in ("kind", "cores", "sample")} | {"value": value, "unit": "TFLOP/s"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_native(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,131 @@
+"""ctypes binding of the C ABI declared in ``include/hilberta_b200.h``.
+
+The shared library is built in-tree (``hilberta_b200/lib/libhilberta_b200.so``,
+see ``hilberta_b200.build``).  There is no fallback: every compute entry of this
+package goes through these symbols, and loading fails loudly when the library
+is missing.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libhilberta_b200.so"
+
+HB_OK = 0
+HB_ERR_ARG = -1
+HB_ERR_ALIGN = -2
+HB_ERR_SHARED = -3
+HB_ERR_CROSS = -4
+HB_ERR_CUDA = -5
+HB_ERR_WORKSPACE = -6
+HB_ERR_UNSUPPORTED = -7
+HB_ERR_DEVICE = -8
+HB_ERR_TMA = -9
+
+HB_DEV_TIMEOUT = 1
+HB_DEV_BAD_COUNT = 2
+HB_DEV_BAD_BLOCK = 4
+
+# Every exported symbol of include/hilberta_b200.h (checked by the CPU tests).
+EXPORTS = (
+    "hb_status_string",
+    "hb_version",
+    "hb_hilbert_order",
+    "hb_plan_dims",
+    "hb_plan_build",
+    "hb_validate_metadata",
+    "hb_pair_metadata",
+    "hb_dense_mask",
+    "hb_fwd_workspace_bytes",
+    "hb_paired_fwd",
+)
+
+
+class PlanDims(ctypes.Structure):
+    _fields_ = [
+        ("image_tokens", ctypes.c_int64),
+        ("image_blocks", ctypes.c_int64),
+        ("total_blocks", ctypes.c_int64),
+        ("text_blocks", ctypes.c_int64),
+        ("shared_blocks", ctypes.c_int64),
+        ("rows", ctypes.c_int64),
+        ("row_capacity", ctypes.c_int64),
+        ("workspace_bytes", ctypes.c_int64),
+    ]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_SIGS = {
+    "hb_status_string": (ctypes.c_char_p, [_I]),
+    "hb_version": (_I, []),
+    "hb_hilbert_order": (_I, [_I, _P, _P]),
+    "hb_plan_dims": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(PlanDims)]),
+    "hb_plan_build": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    "hb_validate_metadata": (_I, [_P, _I64, _I, _P, _I, _I, _I, _P, _P]),
+    "hb_pair_metadata": (_I, [_P, _I64, _P, _I, _I, _I, _I, _P, _P, _I64, _P, _P, _P]),
+    "hb_dense_mask": (_I, [_P, _I64, _P, _I, _I, _I, _I, _P, _P]),
+    "hb_fwd_workspace_bytes": (ctypes.c_size_t, []),
+    "hb_paired_fwd": (
+        _I,
+        [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P, _P],
+    ),
+}
+
+_lib = None
+
+
+class NativeLibraryMissing(RuntimeError):
+    pass
+
+
+def lib():
+    """The loaded library (raises NativeLibraryMissing when it is not built)."""
+    global _lib
+    if _lib is None:
+        path = Path(os.environ.get("HILBERTA_B200_LIB", LIB_PATH))
+        if not path.exists():
+            raise NativeLibraryMissing(
+                f"hilberta_b200 native library not found at {path}; build it with "
+                "`python -c 'import hilberta_b200.build as b; b.build()'`"
+            )
+        handle = ctypes.CDLL(str(path))
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def status_text(code: int) -> str:
+    return lib().hb_status_string(int(code)).decode()
+
+
+def check(code: int, what: str):
+    if code != HB_OK:
+        raise RuntimeError(f"{what} failed: {status_text(code)} (status {code})")
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_ptr(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(device=None) -> torch.device:
+    """The CUDA device the builder runs on; there is no CPU path."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("hilberta_b200 requires a CUDA device (sm_100a); no CPU fallback exists")
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.type != "cuda":
+        raise ValueError("hilberta_b200 builds metadata on a CUDA device")
+    return dev

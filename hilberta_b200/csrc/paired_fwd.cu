@@ -1,0 +1,669 @@
+// Paired block-sparse flash-attention forward for B200 (sm_100a).
+//
+// Computes, for every (batch, head) and every 128-query pair-row, the online-
+// softmax attention over the pair-row's listed 64-key blocks, each block's flag
+// bit h unmasking query half h (rows 64h..64h+63) — the computation of the
+// reference Triton kernel hilberta/paired_kernel.py:18-94 (global pair-rows,
+// rows < G, visit every key block with both flags set, paired_kernel.py:52-57,
+// 71-75; ALL_QUERIES mode).
+//
+// B200 design (one CTA = 8 warps, two CTAs per SM, persistent):
+//   warp 0  item fetcher (atomic work counter, LPT order) + TMA loads of Q, K
+//   warp 1  TMA loads of V
+//   warp 2  single-thread tcgen05.mma issuer: S = Q K^T (SS, 128x64x16 steps)
+//           into TMEM, O += P V (TS: P read from TMEM, V MN-major from SMEM)
+//   warp 3  TMEM allocator
+//   warps 4-7  softmax: one TMEM lane (query row) per thread, exp2 online
+//           softmax with lazy O rescaling (only when the running max grows by
+//           more than 2^8), P written back into the S columns as 16-bit pairs,
+//           epilogue O / l -> global memory.
+// TMEM per CTA: S0 [0,64) S1 [64,128) O [128,128+D) (256 columns; two CTAs fill
+// the 512-column TMEM of an SM).  Tiles use the 128-byte swizzle end to end.
+// Every mbarrier wait is bounded; a timeout sets HB_DEV_TIMEOUT and the CTA
+// drains and exits instead of hanging.  No cluster multicast anywhere.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace hb {
+namespace {
+
+using namespace ptx;
+constexpr unsigned FULL = 0xffffffffu;
+
+struct FwdParams {
+    CUtensorMap tmap_q;
+    CUtensorMap tmap_k;
+    CUtensorMap tmap_v;
+    int32_t perm_q[3], perm_k[3], perm_v[3];  // tensor-map dim (1..3) holding (n, h, b)
+    void* out;
+    int64_t o_sb, o_sh, o_sn;
+    const int32_t* indices;
+    const int32_t* flags;
+    const int32_t* counts;
+    int32_t* ws;  // [0] next work item, [1] finished CTAs, [2] status bits
+    int B, H, N, G, W;
+    int g_rows;          // G / 128 global pair-rows
+    int o_rows;          // (N - G) / 128 ordinary pair-rows
+    int n_global_items;  // B * H * g_rows
+    int num_items;
+    int nkb;  // N / 64 key blocks
+    float scale_log2;
+    long long timeout;  // SM cycles a single barrier wait may take
+};
+
+template <int D>
+struct Cfg {
+    static constexpr int SLABS = D / 64;           // 64-element (128-byte) column slabs
+    static constexpr int Q_SLAB = 128 * 128;       // 128 rows x 128 B
+    static constexpr int KV_SLAB = 64 * 128;       // 64 rows x 128 B
+    static constexpr int Q_BYTES = Q_SLAB * SLABS;
+    static constexpr int KV_BYTES = KV_SLAB * SLABS;
+    static constexpr int KS = 2;  // K stages
+    static constexpr int VS = 2;  // V stages
+    static constexpr int SMEM = Q_BYTES + (KS + VS) * KV_BYTES + 1024;
+    static constexpr int TMEM_COLS = 256;
+    static constexpr uint32_t S_COL0 = 0, O_COL = 128;
+};
+
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8 between rescales
+
+struct Item {
+    int b, h, qrow0, row, n;
+    bool global;
+};
+
+__device__ __forceinline__ Item decode_item(const FwdParams& p, int item, bool report) {
+    Item w;
+    if (item < p.n_global_items) {
+        const int bh = item / p.g_rows;
+        w.b = bh / p.H;
+        w.h = bh % p.H;
+        w.qrow0 = (item % p.g_rows) * 128;
+        w.row = 0;
+        w.n = p.nkb;
+        w.global = true;
+    } else {
+        const int t = item - p.n_global_items;
+        const int bh = t / p.o_rows;
+        w.b = bh / p.H;
+        w.h = bh % p.H;
+        w.row = t % p.o_rows;
+        w.qrow0 = p.G + w.row * 128;
+        const int c = p.counts[w.row];
+        if (report && (c < 1 || c > p.W)) atomicOr(&p.ws[2], HB_DEV_BAD_COUNT);
+        w.n = c < 1 ? 1 : (c > p.W ? p.W : c);
+        w.global = false;
+    }
+    return w;
+}
+
+__device__ __forceinline__ void tma_coords(const int32_t* perm, int n, int h, int b, int& c1, int& c2, int& c3) {
+    c1 = perm[0] == 1 ? n : (perm[1] == 1 ? h : b);
+    c2 = perm[0] == 2 ? n : (perm[1] == 2 ? h : b);
+    c3 = perm[0] == 3 ? n : (perm[1] == 3 ? h : b);
+}
+
+// All 32 lanes poll in lock step so the warp stays converged for the
+// warp-collective tcgen05 loads/stores that follow; bounded like mbar_wait.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, long long limit) {
+    long long t0 = 0;
+    bool started = false;
+    while (true) {
+        const bool ok = mbar_try_wait(bar, parity);
+        if (__all_sync(FULL, ok)) return true;
+        int stop = 0;
+        if ((threadIdx.x & 31) == 0) {
+            if (!started) {
+                t0 = clock64();
+                started = true;
+            }
+            if (*abort_flag || clock64() - t0 > limit) {
+                *abort_flag = 1;
+                stop = 1;
+            }
+        }
+        if (__shfl_sync(FULL, stop, 0)) return false;
+    }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (BF16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    } else {
+        __half2 v = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+}
+
+// Producer of one operand stream (warp-wide; lane 0 issues).  WHICH = 0: Q + K, 1: V.
+template <int D, int WHICH>
+__device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t* bar_item_full,
+                         uint64_t* bar_item_empty, int* item_slot, uint64_t* bar_q_full, uint64_t* bar_q_empty,
+                         uint64_t* bar_full, uint64_t* bar_empty, volatile int* abort_flag) {
+    using C = Cfg<D>;
+    constexpr int STAGES = WHICH == 0 ? C::KS : C::VS;
+    const int lane = threadIdx.x & 31;
+    const CUtensorMap* tmap = WHICH == 0 ? &p.tmap_k : &p.tmap_v;
+    const int32_t* perm = WHICH == 0 ? p.perm_k : p.perm_v;
+    uint32_t gx = 0;  // loads issued over this CTA's lifetime
+    bool ok = true;
+    for (int it = 0; ok; it++) {
+        const int slot = it & 1;
+        int item;
+        if (WHICH == 0) {
+            if (!warp_wait(&bar_item_empty[slot], ((it >> 1) & 1) ^ 1, abort_flag, p.timeout)) break;
+            item = 0;
+            if (lane == 0) {
+                item = atomicAdd(&p.ws[0], 1);
+                item_slot[slot] = item;
+                mbar_arrive(&bar_item_full[slot]);
+            }
+            item = __shfl_sync(FULL, item, 0);
+        } else {
+            if (!warp_wait(&bar_item_full[slot], (it >> 1) & 1, abort_flag, p.timeout)) break;
+            item = item_slot[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_item_empty[slot]);
+        }
+        if (item >= p.num_items) break;
+        const Item w = decode_item(p, item, WHICH == 0 && lane == 0);
+        if (WHICH == 0) {
+            if (!warp_wait(bar_q_empty, (it & 1) ^ 1, abort_flag, p.timeout)) break;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
+                int c1, c2, c3;
+                tma_coords(p.perm_q, w.qrow0, w.h, w.b, c1, c2, c3);
+#pragma unroll
+                for (int s = 0; s < C::SLABS; s++) tma_load_4d(sQ + s * C::Q_SLAB, &p.tmap_q, bar_q_full, 64 * s, c1, c2, c3);
+            }
+        }
+        int chunk = 0;
+        for (int j = 0; j < w.n; j++, gx++) {
+            if (!w.global && (j & 31) == 0) {
+                const int jj = j + lane;
+                chunk = jj < w.n ? p.indices[(int64_t)w.row * p.W + jj] : 0;
+            }
+            const int blk = w.global ? j : __shfl_sync(FULL, chunk, j & 31);
+            const int st = gx % STAGES;
+            if (!warp_wait(&bar_empty[st], ((gx / STAGES) & 1) ^ 1, abort_flag, p.timeout)) {
+                ok = false;
+                break;
+            }
+            if (lane == 0) {
+                int rowc = blk * 64;
+                if (blk < 0 || blk >= p.nkb) {
+                    rowc = p.N;  // fully out of bounds: the TMA unit fills zeros
+                    atomicOr(&p.ws[2], HB_DEV_BAD_BLOCK);
+                }
+                mbar_arrive_expect_tx(&bar_full[st], C::KV_BYTES);
+                int c1, c2, c3;
+                tma_coords(perm, rowc, w.h, w.b, c1, c2, c3);
+#pragma unroll
+                for (int s = 0; s < C::SLABS; s++)
+                    tma_load_4d(sKV + st * C::KV_BYTES + s * C::KV_SLAB, tmap, &bar_full[st], 64 * s, c1, c2, c3);
+            }
+        }
+    }
+    if (*abort_flag) {
+        // Let TMA copies already in flight land in this CTA's shared memory.
+        const long long t0 = clock64();
+        while (clock64() - t0 < (1ll << 22)) {
+        }
+    }
+}
+
+template <int D, bool BF16>
+__device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8_t* sK, uint8_t* sV,
+                           uint64_t* bar_item_full, uint64_t* bar_item_empty, int* item_slot, uint64_t* bar_q_full,
+                           uint64_t* bar_q_empty, uint64_t* bar_k_full, uint64_t* bar_k_empty, uint64_t* bar_v_full,
+                           uint64_t* bar_v_empty, uint64_t* bar_s_full, uint64_t* bar_p_full, uint64_t* bar_o_done,
+                           uint64_t* bar_o_empty, uint64_t* bar_drain, volatile int* abort_flag) {
+    using C = Cfg<D>;
+    constexpr uint32_t IDESC_QK = idesc_f16(128, 64, BF16, false);
+    constexpr uint32_t IDESC_PV = idesc_f16(128, D, BF16, true);
+    const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+    uint32_t g = 0, gk = 0, gv = 0;
+    bool ok = true;
+    for (int it = 0; ok; it++) {
+        const int slot = it & 1;
+        if (!mbar_wait(&bar_item_full[slot], (it >> 1) & 1, abort_flag, p.timeout)) break;
+        const int item = item_slot[slot];
+        mbar_arrive(&bar_item_empty[slot]);
+        if (item >= p.num_items) break;
+        const Item w = decode_item(p, item, false);
+        if (!mbar_wait(bar_q_full, it & 1, abort_flag, p.timeout)) break;
+        tc_fence_after();
+        for (int j = 0; j <= w.n && ok; j++) {
+            if (j < w.n) {  // S_j = Q K_j^T
+                const int st = gk % C::KS;
+                if (!mbar_wait(&bar_k_full[st], (gk / C::KS) & 1, abort_flag, p.timeout)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_s = tmem + C::S_COL0 + ((g + j) & 1) * 64;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint64_t a = desc_sw128(sQa + (kk >> 2) * C::Q_SLAB + (kk & 3) * 32, 16, 1024);
+                    const uint64_t b = desc_sw128(sKa + st * C::KV_BYTES + (kk >> 2) * C::KV_SLAB + (kk & 3) * 32, 16, 1024);
+                    mma_ss(d_s, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
+                }
+                tc_commit(&bar_s_full[(g + j) & 1]);
+                tc_commit(&bar_k_empty[st]);
+                if (j == w.n - 1) tc_commit(bar_q_empty);
+                gk++;
+            }
+            if (j >= 1) {  // O += P_{j-1} V_{j-1}
+                const int jj = j - 1;
+                const uint32_t gg = g + jj;
+                const int buf = gg & 1;
+                if (!mbar_wait(&bar_p_full[buf], (gg >> 1) & 1, abort_flag, p.timeout)) {
+                    ok = false;
+                    break;
+                }
+                if (jj == 0 && !mbar_wait(bar_o_empty, (it & 1) ^ 1, abort_flag, p.timeout)) {
+                    ok = false;
+                    break;
+                }
+                const int sv = gv % C::VS;
+                if (!mbar_wait(&bar_v_full[sv], (gv / C::VS) & 1, abort_flag, p.timeout)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_tmem = tmem + C::S_COL0 + buf * 64;  // P occupies the first 32 columns of S
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint64_t b = desc_sw128(sVa + sv * C::KV_BYTES + kk * 2048, C::KV_SLAB, 1024);
+                    mma_ts(tmem + C::O_COL, a_tmem + kk * 8, b, IDESC_PV, (jj > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc_commit(&bar_v_empty[sv]);
+                tc_commit(bar_o_done);
+                gv++;
+            }
+        }
+        g += w.n;
+    }
+    if (*abort_flag) {  // wait (bounded) for every MMA issued so far before TMEM is released
+        tc_commit(bar_drain);
+        volatile int never = 0;
+        mbar_wait(bar_drain, 0, &never, 1ll << 26);
+    }
+}
+
+template <int D, bool BF16>
+__device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_item_full, uint64_t* bar_item_empty,
+                             int* item_slot, uint64_t* bar_s_full, uint64_t* bar_p_full, uint64_t* bar_o_done,
+                             uint64_t* bar_o_empty, volatile int* abort_flag) {
+    using C = Cfg<D>;
+    const int r = threadIdx.x - 128;  // query row within the tile == TMEM lane
+    const int lane = threadIdx.x & 31;
+    const int half = r >> 6;
+    const uint32_t t_lane = tmem + ((uint32_t)((r >> 5) * 32) << 16);
+    const float sl2 = p.scale_log2;
+    uint32_t g = 0;
+    for (int it = 0;; it++) {
+        const int slot = it & 1;
+        if (!warp_wait(&bar_item_full[slot], (it >> 1) & 1, abort_flag, p.timeout)) return;
+        const int item = item_slot[slot];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_item_empty[slot]);
+        if (item >= p.num_items) return;
+        const Item w = decode_item(p, item, false);
+        float m = -INFINITY, l = 0.f;
+        int chunk = 0;
+        for (int j = 0; j < w.n; j++) {
+            const uint32_t gg = g + j;
+            const int buf = gg & 1;
+            if (!w.global && (j & 31) == 0) {
+                const int jj = j + lane;
+                chunk = jj < w.n ? p.flags[(int64_t)w.row * p.W + jj] : 0;
+            }
+            const int fl = w.global ? 3 : __shfl_sync(FULL, chunk, j & 31);
+            const bool allowed = (fl >> half) & 1;  // uniform per warp
+            if (!warp_wait(&bar_s_full[buf], (gg >> 1) & 1, abort_flag, p.timeout)) return;
+            tc_fence_after();
+            const uint32_t s_addr = t_lane + C::S_COL0 + buf * 64;
+            uint32_t pk[32];
+            float m_new = m, alpha = 1.f;
+            if (allowed) {
+                uint32_t lo[32], hi[32];
+                tmem_ld32(s_addr, lo);
+                tmem_ld32(s_addr + 32, hi);
+                float mx = __uint_as_float(lo[0]);
+#pragma unroll
+                for (int i = 0; i < 32; i++) mx = fmaxf(mx, fmaxf(__uint_as_float(lo[i]), __uint_as_float(hi[i])));
+                mx *= sl2;
+                if (mx > m + RESCALE_THRESHOLD) {
+                    m_new = mx;
+                    alpha = ex2(m - m_new);  // 0 when m == -inf
+                }
+                float sum = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const float p0 = ex2(fmaf(__uint_as_float(lo[2 * i]), sl2, -m_new));
+                    const float p1 = ex2(fmaf(__uint_as_float(lo[2 * i + 1]), sl2, -m_new));
+                    sum += p0 + p1;
+                    pk[i] = pack2<BF16>(p0, p1);
+                }
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const float p0 = ex2(fmaf(__uint_as_float(hi[2 * i]), sl2, -m_new));
+                    const float p1 = ex2(fmaf(__uint_as_float(hi[2 * i + 1]), sl2, -m_new));
+                    sum += p0 + p1;
+                    pk[16 + i] = pack2<BF16>(p0, p1);
+                }
+                l = l * alpha + sum;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) pk[i] = 0u;
+            }
+            tmem_st32(s_addr, pk);
+            // O may only be rescaled once PV_{gg-1} has completed; waiting on every
+            // entry also keeps this thread's o_done phase tracking exact.
+            if (j > 0) {
+                if (!warp_wait(bar_o_done, (gg - 1) & 1, abort_flag, p.timeout)) return;
+                tc_fence_after();
+            }
+            const bool need = (m_new != m) && (m != -INFINITY);
+            if (__any_sync(FULL, need)) {
+                const float a = need ? alpha : 1.f;
+#pragma unroll
+                for (int c = 0; c < D / 32; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(t_lane + C::O_COL + 32 * c, o);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
+                    tmem_st32(t_lane + C::O_COL + 32 * c, o);
+                }
+            }
+            m = m_new;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_p_full[buf]);
+        }
+        // epilogue: O / l -> global
+        const uint32_t gl = g + w.n - 1;
+        if (!warp_wait(bar_o_done, gl & 1, abort_flag, p.timeout)) return;
+        tc_fence_after();
+        const float inv = 1.f / l;
+        using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh +
+                  (int64_t)(w.qrow0 + r) * p.o_sn;
+        const bool vec = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
+#pragma unroll
+        for (int c = 0; c < D / 32; c++) {
+            uint32_t o[32];
+            tmem_ld32(t_lane + C::O_COL + 32 * c, o);
+            uint32_t packed[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                packed[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+            if (vec) {
+                uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+            } else {
+                uint16_t* dst = reinterpret_cast<uint16_t*>(orow + 32 * c);
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    dst[2 * i] = (uint16_t)(packed[i] & 0xffffu);
+                    dst[2 * i + 1] = (uint16_t)(packed[i] >> 16);
+                }
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_o_empty);
+        g += w.n;
+    }
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ FwdParams p) {
+    using C = Cfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + C::Q_BYTES;
+    uint8_t* sV = sK + C::KS * C::KV_BYTES;
+
+    __shared__ __align__(8) uint64_t bar_q_full, bar_q_empty, bar_o_done, bar_o_empty, bar_drain;
+    __shared__ __align__(8) uint64_t bar_k_full[C::KS], bar_k_empty[C::KS], bar_v_full[C::VS], bar_v_empty[C::VS];
+    __shared__ __align__(8) uint64_t bar_s_full[2], bar_p_full[2], bar_item_full[2], bar_item_empty[2];
+    __shared__ int item_slot[2];
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+    volatile int* abort_flag = &abort_sh;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar_q_full, 1);
+        mbar_init(&bar_q_empty, 1);
+        mbar_init(&bar_o_done, 1);
+        mbar_init(&bar_o_empty, 4);
+        mbar_init(&bar_drain, 1);
+        for (int i = 0; i < C::KS; i++) {
+            mbar_init(&bar_k_full[i], 1);
+            mbar_init(&bar_k_empty[i], 1);
+        }
+        for (int i = 0; i < C::VS; i++) {
+            mbar_init(&bar_v_full[i], 1);
+            mbar_init(&bar_v_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&bar_s_full[i], 1);
+            mbar_init(&bar_p_full[i], 4);
+            mbar_init(&bar_item_full[i], 1);
+            mbar_init(&bar_item_empty[i], 6);  // V producer, MMA issuer, 4 softmax warps
+        }
+        abort_sh = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&p.tmap_q);
+        prefetch_tmap(&p.tmap_k);
+        prefetch_tmap(&p.tmap_v);
+    }
+    if (warp == 3) {
+        tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+
+    if (warp == 0) {
+        producer<D, 0>(p, sQ, sK, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_k_full,
+                       bar_k_empty, abort_flag);
+    } else if (warp == 1) {
+        producer<D, 1>(p, sQ, sV, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_v_full,
+                       bar_v_empty, abort_flag);
+    } else if (warp == 2) {
+        if (lane == 0)
+            mma_issuer<D, BF16>(p, tmem, sQ, sK, sV, bar_item_full, bar_item_empty, item_slot, &bar_q_full,
+                                &bar_q_empty, bar_k_full, bar_k_empty, bar_v_full, bar_v_empty, bar_s_full, bar_p_full,
+                                &bar_o_done, &bar_o_empty, &bar_drain, abort_flag);
+    } else if (warp >= 4) {
+        softmax_role<D, BF16>(p, tmem, bar_item_full, bar_item_empty, item_slot, bar_s_full, bar_p_full, &bar_o_done,
+                              &bar_o_empty, abort_flag);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 3) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+    if (threadIdx.x == 0) {
+        if (abort_sh) atomicOr(&p.ws[2], HB_DEV_TIMEOUT);
+        __threadfence();
+        const int prev = atomicAdd(&p.ws[1], 1);
+        if (prev == (int)gridDim.x - 1) {  // last CTA: reset the work counter for the next launch
+            atomicExch(&p.ws[0], 0);
+            atomicExch(&p.ws[1], 0);
+            __threadfence();
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+// [B][H][N][D] view with element strides (sb, sh, sn), D contiguous -> 4-D tiled
+// map (d, then n/h/b sorted by stride), box = 64 x box_rows, 128-byte swizzle.
+int make_tmap(CUtensorMap* map, const void* base, bool bf16, int D, int N, int H, int B, int64_t sb, int64_t sh,
+              int64_t sn, int box_rows, int32_t perm[3]) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return HB_ERR_CUDA;
+    if (reinterpret_cast<uintptr_t>(base) & 15) return HB_ERR_TMA;
+    const int64_t ext[3] = {N, H, B};
+    int64_t strideb[3] = {sn * 2, sh * 2, sb * 2};
+    int64_t span = (int64_t)D * 2;
+    for (int i = 0; i < 3; i++)
+        if (ext[i] > 1) span = std::max<int64_t>(span, ext[i] * strideb[i]);
+    for (int i = 0; i < 3; i++) {
+        if (ext[i] == 1) strideb[i] = (span + 15) & ~int64_t(15);  // never used for addressing
+        if (strideb[i] <= 0 || (strideb[i] & 15) || strideb[i] >= (int64_t(1) << 40)) return HB_ERR_TMA;
+    }
+    int order[3] = {0, 1, 2};
+    for (int a = 0; a < 3; a++)
+        for (int b = a + 1; b < 3; b++)
+            if (strideb[order[b]] < strideb[order[a]] ||
+                (strideb[order[b]] == strideb[order[a]] && order[b] < order[a]))
+                std::swap(order[a], order[b]);
+    cuuint64_t gdim[4], gstride[3];
+    cuuint32_t box[4], estride[4] = {1, 1, 1, 1};
+    gdim[0] = (cuuint64_t)D;
+    box[0] = 64;
+    for (int k = 0; k < 3; k++) {
+        const int dim = order[k];
+        gdim[k + 1] = (cuuint64_t)ext[dim];
+        gstride[k] = (cuuint64_t)strideb[dim];
+        box[k + 1] = dim == 0 ? (cuuint32_t)box_rows : 1u;
+        perm[dim] = k + 1;
+    }
+    const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                           const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? HB_OK : HB_ERR_TMA;
+}
+
+struct DeviceInfo {
+    int sms = 0;
+    bool configured[4] = {false, false, false, false};
+};
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+
+template <int D, bool BF16>
+int launch(const FwdParams& p, int dev, cudaStream_t st) {
+    using C = Cfg<D>;
+    auto kern = k_paired_fwd<D, BF16>;
+    const int slot = (D == 128 ? 2 : 0) + (BF16 ? 1 : 0);
+    int sms;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        DeviceInfo& di = g_dev[dev];
+        if (!di.sms) HB_CUDA_TRY(cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev));
+        if (!di.configured[slot]) {
+            HB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+            di.configured[slot] = true;
+        }
+        sms = di.sms;
+    }
+    const int grid = std::min(p.num_items, 2 * sms);
+    kern<<<grid, 256, C::SMEM, st>>>(p);
+    HB_LAUNCH_CHECK();
+    return HB_OK;
+}
+
+}  // namespace
+}  // namespace hb
+
+using namespace hb;
+
+extern "C" size_t hb_fwd_workspace_bytes(void) { return 64; }
+
+extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides, int B,
+                             int H, int N, int D, int G, int W, int key_block_size, const int32_t* kv_indices,
+                             const int32_t* kv_flags, const int32_t* kv_counts, float scale_log2, int dtype,
+                             void* workspace, void* stream_) {
+    if (!q || !k || !v || !out || !strides || !workspace) return HB_ERR_ARG;
+    if (B <= 0 || H <= 0 || N <= 0 || N % 128 || G < 0 || G % 128 || G >= N || W < 1) return HB_ERR_ARG;
+    if (D != 64 && D != 128) return HB_ERR_UNSUPPORTED;
+    if (key_block_size != 64) return HB_ERR_UNSUPPORTED;
+    if (dtype != 0 && dtype != 1) return HB_ERR_UNSUPPORTED;
+    if (!(scale_log2 > 0.f) || scale_log2 == INFINITY) return HB_ERR_ARG;
+    const int o_rows = (N - G) / 128;
+    if (o_rows > 0 && (!kv_indices || !kv_flags || !kv_counts)) return HB_ERR_ARG;
+    const int64_t items = (int64_t)B * H * (N / 128);
+    if (items > INT32_MAX / 2) return HB_ERR_UNSUPPORTED;
+    int dev;
+    HB_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return HB_ERR_UNSUPPORTED;
+
+    FwdParams p;
+    memset(&p, 0, sizeof(p));
+    const bool bf16 = dtype == 1;
+    int rc;
+    if ((rc = make_tmap(&p.tmap_q, q, bf16, D, N, H, B, strides[0], strides[1], strides[2], 128, p.perm_q))) return rc;
+    if ((rc = make_tmap(&p.tmap_k, k, bf16, D, N, H, B, strides[3], strides[4], strides[5], 64, p.perm_k))) return rc;
+    if ((rc = make_tmap(&p.tmap_v, v, bf16, D, N, H, B, strides[6], strides[7], strides[8], 64, p.perm_v))) return rc;
+    p.out = out;
+    p.o_sb = strides[9];
+    p.o_sh = strides[10];
+    p.o_sn = strides[11];
+    p.indices = kv_indices;
+    p.flags = kv_flags;
+    p.counts = kv_counts;
+    p.ws = reinterpret_cast<int32_t*>(workspace);
+    p.B = B;
+    p.H = H;
+    p.N = N;
+    p.G = G;
+    p.W = W;
+    p.g_rows = G / 128;
+    p.o_rows = o_rows;
+    p.n_global_items = B * H * p.g_rows;
+    p.num_items = (int)items;
+    p.nkb = N / 64;
+    p.scale_log2 = scale_log2;
+    p.timeout = 2000000000ll;
+    cudaStream_t st = (cudaStream_t)stream_;
+    if (D == 128) return bf16 ? launch<128, true>(p, dev, st) : launch<128, false>(p, dev, st);
+    return bf16 ? launch<64, true>(p, dev, st) : launch<64, false>(p, dev, st);
+}

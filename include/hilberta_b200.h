@@ -1,0 +1,147 @@
+/*
+ * hilberta_b200 — C ABI of the B200 (sm_100a) HilbertA inference attention path.
+ *
+ * Plain pointers, sizes and a CUDA stream (passed as void*); no torch types.
+ * Every function returns 0 on success or a negative HB_ERR_* code; none of them
+ * allocates or frees device memory (callers pass every buffer) and none of them
+ * synchronises the stream except where stated.  Device pointers must be on the
+ * current CUDA device.
+ *
+ * Reference interfaces replaced (wenboluu/hilberta, path:line):
+ *   hb_hilbert_order               hilberta/geometry.py:6-25 (hilbert_order)
+ *   hb_plan_dims / hb_plan_build   hilberta/plan.py:114-197 (build_plan),
+ *                                  hilberta/bridge_k.py:10-51 (bridge_k_plan),
+ *                                  hilberta/geometry.py:6-43 (hilbert_order, neighbor_pairs)
+ *   hb_validate_metadata           hilberta/sparse_kernel.py:100-152 (validate_metadata)
+ *   hb_pair_metadata               hilberta/paired_metadata.py:26-51 (pair_metadata)
+ *   hb_dense_mask                  hilberta/plan.py:70-84 (AttentionPlan.dense_mask),
+ *                                  hilberta/sparse_kernel.py:155-166 (explicit_mask)
+ *   hb_paired_fwd                  hilberta/paired_kernel.py:18-94 (_paired_fwd Triton kernel)
+ *                                  launched by paired_kernel.py:97-205 (paired_attention)
+ */
+#ifndef HILBERTA_B200_H
+#define HILBERTA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define HB_OK 0
+#define HB_ERR_ARG -1          /* invalid argument (ValueError in the Python layer)      */
+#define HB_ERR_ALIGN -2        /* block/tile alignment precondition violated             */
+#define HB_ERR_SHARED -3       /* shared square is not a union of complete blocks        */
+#define HB_ERR_CROSS -4        /* a physical block crosses a tile boundary               */
+#define HB_ERR_CUDA -5         /* a CUDA runtime call failed                             */
+#define HB_ERR_WORKSPACE -6    /* workspace too small                                    */
+#define HB_ERR_UNSUPPORTED -7  /* shape/dtype outside the compiled kernels               */
+#define HB_ERR_DEVICE -8       /* kernel-reported device status (see hb_fwd_status_*)    */
+#define HB_ERR_TMA -9          /* tensor-map encoding rejected the strides/alignment     */
+
+/* device status bits written by hb_paired_fwd into workspace[2] */
+#define HB_DEV_TIMEOUT 1       /* a bounded barrier wait ran out; the kernel returned    */
+#define HB_DEV_BAD_COUNT 2     /* kv_counts entry outside [0, W]; clamped                */
+#define HB_DEV_BAD_BLOCK 4     /* kv_indices entry outside [0, N/64); its tile read zeros */
+
+/* Human-readable text for a status code (static storage). */
+const char* hb_status_string(int code);
+
+/* Library/ABI version: major*10000 + minor*100 + patch. */
+int hb_version(void);
+
+/* ---- metadata builder -------------------------------------------------- */
+/* Raster id of the d-th cell of the Hilbert walk, vertically flipped, for
+ * d in [0, grid^2) (geometry.py:6-25).  out: int64 [grid^2] on the device. */
+int hb_hilbert_order(int grid_size, int64_t* out, void* stream);
+
+typedef struct hb_plan_dims_t {
+    int64_t image_tokens;    /* n = grid^2                                          */
+    int64_t image_blocks;    /* nb = n / block                                      */
+    int64_t total_blocks;    /* (text + n) / block                                  */
+    int64_t text_blocks;     /* text / block                                        */
+    int64_t shared_blocks;   /* blocks of the shared square (0 when shared == 0)    */
+    int64_t rows;            /* ordinary query blocks = nb - shared_blocks          */
+    int64_t row_capacity;    /* kv_indices row stride the builder writes (= total)  */
+    int64_t workspace_bytes; /* scratch hb_plan_build needs                         */
+} hb_plan_dims_t;
+
+/* Host-only: validate the build_plan preconditions (plan.py:117-132) and size
+ * the outputs.  HB_ERR_ARG for non-positive / non-power-of-two / grid < 8,
+ * HB_ERR_ALIGN for the tile-quarter / text alignment rule. */
+int hb_plan_dims(int grid_size, int tile_count, int text_tokens, int block_size, int shared,
+                 hb_plan_dims_t* out);
+
+/* Build a plan on the device.
+ *   bridge_k  : 0 = no bridge (build_plan bridge=False), 1..4 = top-K bridges.
+ *   reciprocal: 0 = build_plan semantics (K must be 0 or 1, directed bridge),
+ *               1 = bridge_k_plan semantics (adjacency closed under transpose).
+ * Outputs (device, caller-allocated):
+ *   image_order, inverse_image_order, original_order : int64 [n]
+ *   physical_original_blocks                          : int64 [nb]
+ *   kv_indices : int32 [4][rows][row_capacity] (ascending ids, zero padded)
+ *   kv_counts  : int32 [4][rows]
+ *   bridge_original_blocks : int64 [4][nb][max(1,bridge_k)] (-1 padded)
+ *   info       : int32 [8]  ([0] status (HB_ERR_SHARED/HB_ERR_CROSS or 0),
+ *                            [1] shared block count, [2..5] max kv count per phase)
+ * Enqueued on `stream`; the caller synchronises before reading info. */
+int hb_plan_build(int grid_size, int tile_count, int text_tokens, int block_size, int shared,
+                  int bridge_k, int reciprocal, int64_t* image_order, int64_t* inverse_image_order,
+                  int64_t* original_order, int64_t* physical_original_blocks, int32_t* kv_indices,
+                  int32_t* kv_counts, int64_t* bridge_original_blocks, int32_t* info,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Device-side validate_metadata (sparse_kernel.py:100-152) for 64-token blocks.
+ * kv_indices int32 [rows][ld], kv_counts int32 [rows].  result[0] receives
+ * INT32_MAX when valid, else row*4 + code with code 1 = count outside [1, width],
+ * 2 = out-of-range or duplicate id, 3 = a global-prefix block missing (the first
+ * failing row, first failing check, in the reference's order).  result[1..3]
+ * receive min count, max count and the sum of counts.  `result` must be
+ * initialised by hb_validate_metadata itself (it writes the identities first). */
+int hb_validate_metadata(const int32_t* kv_indices, int64_t ld, int32_t width, const int32_t* kv_counts,
+                         int32_t rows, int32_t tokens, int32_t global_tokens, int32_t* result,
+                         void* stream);
+
+/* Paired metadata (paired_metadata.py:26-51) of already-validated rows.
+ * out_ids / out_flags int32 [rows/2][ld_out] (zero padded), out_counts int32 [rows/2],
+ * info[0] <- max paired count.  key_block_size 64 or 128. */
+int hb_pair_metadata(const int32_t* kv_indices, int64_t ld, const int32_t* kv_counts, int32_t rows,
+                     int32_t tokens, int32_t global_tokens, int32_t key_block_size, int32_t* out_ids,
+                     int32_t* out_flags, int64_t ld_out, int32_t* out_counts, int32_t* info,
+                     void* stream);
+
+/* Token-level bool mask [tokens][tokens] (uint8 0/1) of 64-token (block_size) rows:
+ * rows < global_tokens all 1, ordinary rows their listed blocks (plan.py:70-84). */
+int hb_dense_mask(const int32_t* kv_indices, int64_t ld, const int32_t* kv_counts, int32_t rows,
+                  int32_t tokens, int32_t global_tokens, int32_t block_size, uint8_t* mask,
+                  void* stream);
+
+/* ---- paired block-sparse attention forward ------------------------------ */
+/* Bytes of the per-stream scheduler workspace hb_paired_fwd needs.  It must be
+ * zeroed once before first use; the kernel leaves it zeroed (self-resetting)
+ * except for the status word workspace[2], which accumulates HB_DEV_* bits until
+ * the caller clears it.  Launches that may overlap on the device must use
+ * different workspaces. */
+size_t hb_fwd_workspace_bytes(void);
+
+/* O = softmax(Q K^T * scale | mask) V over the paired metadata, one launch.
+ *   q,k,v,out : [B][H][N][D] with element strides strides[t*3 + {0,1,2}] = (b,h,n)
+ *               for t = 0 q, 1 k, 2 v, 3 out; the D stride is 1.
+ *   dtype     : 0 = fp16, 1 = bf16.   D: 64 or 128.   key_block_size: 64.
+ *   G         : global (fully connected) query prefix, a multiple of 128, < N.
+ *   kv_indices/kv_flags int32 [(N-G)/128][W], kv_counts int32 [(N-G)/128]
+ *               (device, contiguous, validated).
+ *   scale_log2 = softmax scale * log2(e).
+ * Global rows (< G) attend every key block; ordinary pair-rows their listed
+ * blocks, each flag bit h unmasking query half h.  Asynchronous on `stream`. */
+int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides,
+                  int B, int H, int N, int D, int G, int W, int key_block_size,
+                  const int32_t* kv_indices, const int32_t* kv_flags, const int32_t* kv_counts,
+                  float scale_log2, int dtype, void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HILBERTA_B200_H */

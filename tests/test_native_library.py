@@ -1,0 +1,76 @@
+"""The C-ABI library builds for sm_100a, loads without a GPU, and exports every
+symbol ``include/hilberta_b200.h`` declares; host-only entry points behave."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from hilberta_b200 import _lib, build
+
+    build.build()
+    return _lib.lib()
+
+
+def test_header_symbols_are_exported(lib):
+    from hilberta_b200 import _lib
+
+    header = (ROOT / "include" / "hilberta_b200.h").read_text()
+    declared = set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(hb_\w+)\s*\(", header, re.M))
+    assert declared, "no declarations parsed"
+    assert declared == set(_lib.EXPORTS)
+    for name in declared:
+        assert getattr(lib, name) is not None
+
+
+def test_status_strings(lib):
+    from hilberta_b200 import _lib
+
+    assert _lib.status_text(0) == "ok"
+    assert "Shared square" in _lib.status_text(_lib.HB_ERR_SHARED)
+    assert lib.hb_version() >= 100
+    assert lib.hb_fwd_workspace_bytes() >= 12
+
+
+def test_plan_dims_preconditions(lib):
+    from hilberta_b200 import _lib
+
+    d = _lib.PlanDims()
+    assert lib.hb_plan_dims(128, 16, 512, 64, 0, ctypes.byref(d)) == 0
+    assert (d.image_tokens, d.image_blocks, d.rows, d.total_blocks) == (16384, 256, 256, 264)
+    assert lib.hb_plan_dims(64, 4, 512, 64, 1, ctypes.byref(d)) == 0
+    assert d.shared_blocks == 4 and d.rows == 60
+    assert lib.hb_plan_dims(12, 4, 512, 64, 0, ctypes.byref(d)) == _lib.HB_ERR_ARG
+    assert lib.hb_plan_dims(64, 16, 512, 128, 0, ctypes.byref(d)) == _lib.HB_ERR_ALIGN  # test_plan.py:65-69
+    assert lib.hb_plan_dims(64, 4, 17, 64, 0, ctypes.byref(d)) == _lib.HB_ERR_ALIGN
+
+
+def test_invalid_arguments_rejected_before_any_launch(lib):
+    from hilberta_b200 import _lib
+
+    null = None
+    assert lib.hb_paired_fwd(null, null, null, null, null, 1, 1, 256, 128, 0, 1, 64, null, null, null, 1.0, 1, null, null) == _lib.HB_ERR_ARG
+    strides = (ctypes.c_int64 * 12)(*([1] * 12))
+    fake = ctypes.c_void_p(1 << 20)
+    # D = 96 unsupported, key block 128 unsupported, N not a multiple of 128
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 96, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, null) == _lib.HB_ERR_UNSUPPORTED
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 128, fake, fake, fake, 1.0, 1, fake, null) == _lib.HB_ERR_UNSUPPORTED
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 200, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, null) == _lib.HB_ERR_ARG
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 256, 1, 64, fake, fake, fake, 1.0, 1, fake, null) == _lib.HB_ERR_ARG
+    assert lib.hb_pair_metadata(fake, 4, fake, 3, 512, 128, 64, fake, fake, 8, fake, fake, null) == _lib.HB_ERR_ARG
+    assert lib.hb_validate_metadata(fake, 2, 4, fake, 3, 512, 128, fake, null) == _lib.HB_ERR_ARG
+
+
+def test_build_entry_compiles_for_sm100a():
+    from hilberta_b200 import build
+
+    assert "arch=compute_100a,code=sm_100a" in build.FLAGS
+    assert build.OUT.exists()
