@@ -98,16 +98,17 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
 
 // Physical block order = shared blocks then ordinary blocks, each ascending by
 // original id (plan.py:145-150).  packed[p] = original id; o2p[kb] = physical
-// block id (text blocks first).  One CTA of 1024 threads.
+// block id (text blocks first).  One CTA of 1024 threads.  Straddling blocks
+// (an error the host reports from info[0]) are packed with the ordinary ones so
+// that packed / o2p stay permutations and no later kernel indexes out of range.
 __global__ void k_pack(int64_t nb, int64_t text_blocks, const int32_t* __restrict__ share,
                        int64_t* __restrict__ packed, int32_t* __restrict__ o2p, int32_t* __restrict__ info) {
     __shared__ int warp_sums[32];
     int base = 0;
     for (int pass = 0; pass < 2; pass++) {
-        const int want = pass == 0 ? 1 : 0;
         for (int64_t c = 0; c < nb; c += blockDim.x) {
             const int64_t kb = c + threadIdx.x;
-            const int f = (kb < nb && share[kb] == want) ? 1 : 0;
+            const int f = (kb < nb && ((share[kb] == 1) == (pass == 0))) ? 1 : 0;
             int total;
             const int pos = base + block_exclusive_scan(f, warp_sums, &total);
             if (f) {
@@ -357,7 +358,7 @@ __global__ void k_pair(const int32_t* __restrict__ ids, int64_t ld, const int32_
         const int c = counts[r];
         for (int i = threadIdx.x; i < c; i += blockDim.x) {
             const int blk = ids[r * ld + i];
-            atomicOr(&fl[blk / ratio], 1 << (half + 2 * (blk % ratio)));
+            if (blk >= 0 && blk / ratio < nkb) atomicOr(&fl[blk / ratio], 1 << (half + 2 * (blk % ratio)));
         }
     }
     __syncthreads();
@@ -382,7 +383,10 @@ __global__ void k_dense_mask(const int32_t* __restrict__ ids, int64_t ld, const 
     if (rb >= gbr) {
         const int r = rb - gbr;
         const int c = counts[r];
-        for (int i = threadIdx.x; i < c; i += blockDim.x) allowed[ids[(int64_t)r * ld + i]] = 1;
+        for (int i = threadIdx.x; i < c; i += blockDim.x) {
+            const int id = ids[(int64_t)r * ld + i];
+            if (id >= 0 && id < nbc) allowed[id] = 1;
+        }
     }
     __syncthreads();
     for (int rr = 0; rr < bs; rr++) {

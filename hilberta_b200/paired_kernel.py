@@ -30,7 +30,8 @@ def _workspace(device: torch.device, stream_handle: int) -> torch.Tensor:
     ws = _workspaces.get(key)
     if ws is None:
         n = max(16, _lib.lib().hb_fwd_workspace_bytes() // 4)
-        ws = torch.zeros(n, dtype=torch.int32, device=device)
+        with torch.inference_mode(False):  # a normal tensor: device_status clears it in place
+            ws = torch.zeros(n, dtype=torch.int32, device=device)
         _workspaces[key] = ws
     return ws
 
