@@ -43,6 +43,7 @@ EXPORTS = (
     "hb_dense_mask",
     "hb_fwd_workspace_bytes",
     "hb_paired_fwd",
+    "hb_paired_fwd_noalloc",
 )
 
 
@@ -75,6 +76,10 @@ _SIGS = {
     "hb_paired_fwd": (
         _I,
         [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P, _P],
+    ),
+    "hb_paired_fwd_noalloc": (
+        _I,
+        [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P],
     ),
 }
 

@@ -667,3 +667,52 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
     if (D == 128) return bf16 ? launch<128, true>(p, dev, st) : launch<128, false>(p, dev, st);
     return bf16 ? launch<64, true>(p, dev, st) : launch<64, false>(p, dev, st);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.  For callers that cannot allocate device memory
+// (runtime plugins that may not allocate while enqueueing, fixed-budget
+// real-time hosts, bindings without a CUDA allocator): the scheduler words of
+// the kernel live in this file-scope array instead of a caller workspace.
+// Every GPU that loads the library holds its own copy until the process exits;
+// all calls on a device share it, so overlapping calls race.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) int32_t hb_noalloc_scratch[HB_NOALLOC_SCRATCH_BYTES / 4];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Host code may not pass `hb_noalloc_scratch` itself to a kernel (on the host it
+// names a stand-in, not device memory): look the device address up once per
+// device, with that device current.
+int noalloc_scratch(int dev, void** out) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, hb_noalloc_scratch) != cudaSuccess || !p) return HB_ERR_CUDA;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return HB_OK;
+}
+}  // namespace
+
+extern "C" int hb_paired_fwd_noalloc(const void* q, const void* k, const void* v, void* out, const int64_t* strides,
+                                     int B, int H, int N, int D, int G, int W, int key_block_size,
+                                     const int32_t* kv_indices, const int32_t* kv_flags, const int32_t* kv_counts,
+                                     float scale_log2, int dtype, void* stream) {
+    if (B <= 0 || H <= 0 || N <= 0 || N % 128) return HB_ERR_ARG;
+    if ((int64_t)B * H * (N / 128) > (int64_t)HB_NOALLOC_MAX_ITEMS) return HB_ERR_UNSUPPORTED;
+    if (hb_fwd_workspace_bytes() > (size_t)HB_NOALLOC_SCRATCH_BYTES) return HB_ERR_WORKSPACE;
+    int dev;
+    HB_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return HB_ERR_UNSUPPORTED;
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(dev, &scratch);
+    if (rc) return rc;
+    // The work counter and finished-CTA counter must start at zero; the array
+    // keeps whatever the previous call left, so clear it on the call's stream.
+    HB_CUDA_TRY(cudaMemsetAsync(scratch, 0, hb_fwd_workspace_bytes(), (cudaStream_t)stream));
+    return hb_paired_fwd(q, k, v, out, strides, B, H, N, D, G, W, key_block_size, kv_indices, kv_flags, kv_counts,
+                         scale_log2, dtype, scratch, stream);
+}

@@ -141,6 +141,33 @@ int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const 
                   const int32_t* kv_indices, const int32_t* kv_flags, const int32_t* kv_counts,
                   float scale_log2, int dtype, void* workspace, void* stream);
 
+/* ---- allocation-free variant of hb_paired_fwd --------------------------- */
+/* No counterpart in the reference: an addition for callers that must not
+ * allocate device memory.  Some hosts cannot call cudaMalloc from the thread
+ * that enqueues work: plugin interfaces of inference runtimes that own every
+ * device allocation and forbid allocating while enqueueing, real-time services
+ * that fix their memory budget at start-up, and language bindings that have no
+ * CUDA allocator to hand the per-stream workspace hb_paired_fwd expects.
+ *
+ * Same arguments and result as hb_paired_fwd, minus `workspace`: the scheduler
+ * words live in a library-owned static device array of
+ * HB_NOALLOC_SCRATCH_BYTES bytes, one per GPU that loads the library, held
+ * until the process exits.  The first call on a device looks the array's
+ * address up (cudaGetSymbolAddress, with that device current); make that first
+ * call before any stream capture.  Each call clears the words it uses
+ * (cudaMemsetAsync, no allocation) and then launches the same kernel as
+ * hb_paired_fwd.  All calls share the one array, so calls that may overlap on
+ * the GPU (different streams, no ordering between them) race; serialise them
+ * or use hb_paired_fwd with separate workspaces.  Device status bits are not
+ * reported by this variant.  Problems needing more than HB_NOALLOC_MAX_ITEMS
+ * work items (B*H*N/128) are rejected with HB_ERR_UNSUPPORTED. */
+#define HB_NOALLOC_SCRATCH_BYTES 256
+#define HB_NOALLOC_MAX_ITEMS (1 << 30)
+int hb_paired_fwd_noalloc(const void* q, const void* k, const void* v, void* out,
+                          const int64_t* strides, int B, int H, int N, int D, int G, int W,
+                          int key_block_size, const int32_t* kv_indices, const int32_t* kv_flags,
+                          const int32_t* kv_counts, float scale_log2, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
