@@ -77,6 +77,13 @@ struct Cfg {
 };
 
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8 between rescales
+// One in POLY_EXP2_EVERY element pairs of a score row takes 2^x from ex2_poly2
+// (FMA pipe) instead of MUFU ex2; a power of two, 0 = MUFU only (measured
+// fastest while the kernel is latency- rather than MUFU-bound).
+#ifndef HB_POLY_EXP2_EVERY
+#define HB_POLY_EXP2_EVERY 0
+#endif
+constexpr int POLY_EXP2_EVERY = HB_POLY_EXP2_EVERY;
 
 struct Item {
     int b, h, qrow0, row, n;
@@ -234,7 +241,12 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
     using C = Cfg<D>;
     constexpr uint32_t IDESC_QK = idesc_f16(128, 64, BF16, false);
     constexpr uint32_t IDESC_PV = idesc_f16(128, D, BF16, true);
-    const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+    // Descriptor bases built once; each MMA adds a compile-time (offset >> 4) to
+    // the 14-bit start-address field (shared addresses stay below 2^18, so the
+    // field never carries).
+    const uint64_t dq0 = desc_sw128(smem_u32(sQ), 16, 1024);
+    const uint64_t dk0 = desc_sw128(smem_u32(sK), 16, 1024);
+    const uint64_t dv0 = desc_sw128(smem_u32(sV), C::KV_SLAB, 1024);
     uint32_t g = 0, gk = 0, gv = 0;
     bool ok = true;
     for (int it = 0; ok; it++) {
@@ -255,10 +267,11 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
                 }
                 tc_fence_after();
                 const uint32_t d_s = tmem + C::S_COL0 + ((g + j) & 1) * 64;
+                const uint64_t dk_st = dk0 + (uint64_t)((st * C::KV_BYTES) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
-                    const uint64_t a = desc_sw128(sQa + (kk >> 2) * C::Q_SLAB + (kk & 3) * 32, 16, 1024);
-                    const uint64_t b = desc_sw128(sKa + st * C::KV_BYTES + (kk >> 2) * C::KV_SLAB + (kk & 3) * 32, 16, 1024);
+                    const uint64_t a = dq0 + (uint64_t)(((kk >> 2) * C::Q_SLAB + (kk & 3) * 32) >> 4);
+                    const uint64_t b = dk_st + (uint64_t)(((kk >> 2) * C::KV_SLAB + (kk & 3) * 32) >> 4);
                     mma_ss(d_s, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
                 }
                 tc_commit(&bar_s_full[(g + j) & 1]);
@@ -287,7 +300,7 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
                 const uint32_t a_tmem = tmem + C::S_COL0 + buf * 64;  // P occupies the first 32 columns of S
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++) {
-                    const uint64_t b = desc_sw128(sVa + sv * C::KV_BYTES + kk * 2048, C::KV_SLAB, 1024);
+                    const uint64_t b = dv0 + (uint64_t)((sv * C::KV_BYTES + kk * 2048) >> 4);
                     mma_ts(tmem + C::O_COL, a_tmem + kk * 8, b, IDESC_PV, (jj > 0 || kk > 0) ? 1u : 0u);
                 }
                 tc_commit(&bar_v_empty[sv]);
@@ -340,33 +353,49 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             uint32_t pk[32];
             float m_new = m, alpha = 1.f;
             if (allowed) {
-                uint32_t lo[32], hi[32];
-                tmem_ld32(s_addr, lo);
-                tmem_ld32(s_addr + 32, hi);
-                float mx = __uint_as_float(lo[0]);
+                uint32_t s[64];
+                tmem_ld64(s_addr, s);
+                // row max: 3-input max over four independent chains
+                float a0 = fmaxf(__uint_as_float(s[0]), __uint_as_float(s[1]));
+                float a1 = fmaxf(__uint_as_float(s[2]), __uint_as_float(s[3]));
+                float a2 = fmaxf(__uint_as_float(s[4]), __uint_as_float(s[5]));
+                float a3 = fmaxf(__uint_as_float(s[6]), __uint_as_float(s[7]));
 #pragma unroll
-                for (int i = 0; i < 32; i++) mx = fmaxf(mx, fmaxf(__uint_as_float(lo[i]), __uint_as_float(hi[i])));
-                mx *= sl2;
+                for (int i = 8; i < 64; i += 8) {
+                    a0 = fmax3(a0, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+                    a1 = fmax3(a1, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
+                    a2 = fmax3(a2, __uint_as_float(s[i + 4]), __uint_as_float(s[i + 5]));
+                    a3 = fmax3(a3, __uint_as_float(s[i + 6]), __uint_as_float(s[i + 7]));
+                }
+                const float mx = fmaxf(fmax3(a0, a1, a2), a3) * sl2;
                 if (mx > m + RESCALE_THRESHOLD) {
                     m_new = mx;
                     alpha = ex2(m - m_new);  // 0 when m == -inf
                 }
-                float sum = 0.f;
+                // p = 2^(s*scale*log2e - m): packed FMA for the argument, MUFU ex2,
+                // packed adds into four partial row sums
+                const uint64_t scale2 = f2_pack(sl2, sl2);
+                const uint64_t neg_m2 = f2_pack(-m_new, -m_new);
+                uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const float p0 = ex2(fmaf(__uint_as_float(lo[2 * i]), sl2, -m_new));
-                    const float p1 = ex2(fmaf(__uint_as_float(lo[2 * i + 1]), sl2, -m_new));
-                    sum += p0 + p1;
+                for (int i = 0; i < 32; i++) {
+                    const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
+                                               scale2, neg_m2);
+                    float x0, x1, p0, p1;
+                    f2_unpack(x2, x0, x1);
+                    if (POLY_EXP2_EVERY > 0 && (i & (POLY_EXP2_EVERY - 1)) == POLY_EXP2_EVERY - 1) {
+                        ex2_poly2(x0, x1, p0, p1);
+                    } else {
+                        p0 = ex2(x0);
+                        p1 = ex2(x1);
+                    }
+                    acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
                     pk[i] = pack2<BF16>(p0, p1);
                 }
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const float p0 = ex2(fmaf(__uint_as_float(hi[2 * i]), sl2, -m_new));
-                    const float p1 = ex2(fmaf(__uint_as_float(hi[2 * i + 1]), sl2, -m_new));
-                    sum += p0 + p1;
-                    pk[16 + i] = pack2<BF16>(p0, p1);
-                }
-                l = l * alpha + sum;
+                float s0, s1, s2, s3;
+                f2_unpack(f2_add(acc[0], acc[1]), s0, s1);
+                f2_unpack(f2_add(acc[2], acc[3]), s2, s3);
+                l = l * alpha + ((s0 + s1) + (s2 + s3));
             } else {
 #pragma unroll
                 for (int i = 0; i < 32; i++) pk[i] = 0u;
