@@ -42,6 +42,7 @@ EXPORTS = (
     "hb_pair_metadata",
     "hb_dense_mask",
     "hb_fwd_workspace_bytes",
+    "hb_fwd_workspace_bytes_for",
     "hb_paired_fwd",
     "hb_paired_fwd_noalloc",
 )
@@ -73,9 +74,11 @@ _SIGS = {
     "hb_pair_metadata": (_I, [_P, _I64, _P, _I, _I, _I, _I, _P, _P, _I64, _P, _P, _P]),
     "hb_dense_mask": (_I, [_P, _I64, _P, _I, _I, _I, _I, _P, _P]),
     "hb_fwd_workspace_bytes": (ctypes.c_size_t, []),
+    "hb_fwd_workspace_bytes_for": (ctypes.c_size_t, [_I, _I, _I, _I, _I]),
     "hb_paired_fwd": (
         _I,
-        [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P, _P],
+        [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P,
+         ctypes.c_size_t, _P],
     ),
     "hb_paired_fwd_noalloc": (
         _I,

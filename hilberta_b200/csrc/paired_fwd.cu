@@ -55,12 +55,24 @@ struct FwdParams {
     int B, H, N, G, W;
     int g_rows;          // G / 128 global pair-rows
     int o_rows;          // (N - G) / 128 ordinary pair-rows
-    int n_global_items;  // B * H * g_rows
+    int n_global_items;  // B * H * g_rows * n_chunks
     int num_items;
     int nkb;  // N / 64 key blocks
+    // Split of the global pair-rows over their key blocks (n_chunks == 1: none):
+    // chunk c covers blocks [c*chunk, min(nkb, (c+1)*chunk)) and leaves O, m, l of
+    // its 128 rows in `partial`; the last chunk of a row merges them.
+    int chunk, n_chunks;
+    float* partial;      // [B*H*g_rows][n_chunks][128*D + 256] fp32
+    int32_t* chunk_cnt;  // [B*H*g_rows] finished chunks (reset to 0 by the merger)
     float scale_log2;
     long long timeout;  // SM cycles a single barrier wait may take
 };
+
+// Scratch layout of the workspace, in bytes: header (scheduler words), chunk
+// counters, then the chunk partials.
+constexpr int64_t WS_HEADER = 256;
+constexpr int MAX_CHUNKS = 32;
+constexpr int CHUNK_BLOCKS = 32;  // target key blocks per chunk of a global pair-row
 
 template <int D>
 struct Cfg {
@@ -87,20 +99,35 @@ constexpr int POLY_EXP2_EVERY = HB_POLY_EXP2_EVERY;
 
 struct Item {
     int b, h, qrow0, row, n;
-    bool global;
+    int blk0;         // global rows: first key block of this chunk
+    int chunk, group; // global rows: chunk index, (b*H + h)*g_rows + global pair-row
+    bool global, split;
 };
 
 __device__ __forceinline__ Item decode_item(const FwdParams& p, int item, bool report) {
     Item w;
     if (item < p.n_global_items) {
-        const int bh = item / p.g_rows;
+        // (bh, chunk, global pair-row): the global rows reading the same key blocks
+        // of one head run back to back, so those K/V blocks are served from L2
+        const int gp = item % p.g_rows;
+        const int t = item / p.g_rows;
+        const int c = t % p.n_chunks;
+        const int bh = t / p.n_chunks;
         w.b = bh / p.H;
         w.h = bh % p.H;
-        w.qrow0 = (item % p.g_rows) * 128;
+        w.qrow0 = gp * 128;
         w.row = 0;
-        w.n = p.nkb;
+        w.blk0 = c * p.chunk;
+        w.n = min(p.chunk, p.nkb - w.blk0);
+        w.chunk = c;
+        w.group = bh * p.g_rows + gp;
         w.global = true;
+        w.split = p.n_chunks > 1;
     } else {
+        w.blk0 = 0;
+        w.chunk = 0;
+        w.group = 0;
+        w.split = false;
         const int t = item - p.n_global_items;
         const int bh = t / p.o_rows;
         w.b = bh / p.H;
@@ -203,7 +230,7 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
                 const int jj = j + lane;
                 chunk = jj < w.n ? p.indices[(int64_t)w.row * p.W + jj] : 0;
             }
-            const int blk = w.global ? j : __shfl_sync(FULL, chunk, j & 31);
+            const int blk = w.global ? w.blk0 + j : __shfl_sync(FULL, chunk, j & 31);
             const int st = gx % STAGES;
             if (!warp_wait(&bar_empty[st], ((gx / STAGES) & 1) ^ 1, abort_flag, p.timeout)) {
                 ok = false;
@@ -320,9 +347,10 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
 template <int D, bool BF16>
 __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_item_full, uint64_t* bar_item_empty,
                              int* item_slot, uint64_t* bar_s_full, uint64_t* bar_p_full, uint64_t* bar_o_done,
-                             uint64_t* bar_o_empty, volatile int* abort_flag) {
+                             uint64_t* bar_o_empty, uint64_t* bar_wg, int* wg_flag, volatile int* abort_flag) {
     using C = Cfg<D>;
     const int r = threadIdx.x - 128;  // query row within the tile == TMEM lane
+    uint32_t wg_uses = 0;             // phases of bar_wg (the 4 softmax warps) used so far
     const int lane = threadIdx.x & 31;
     const int half = r >> 6;
     const uint32_t t_lane = tmem + ((uint32_t)((r >> 5) * 32) << 16);
@@ -425,23 +453,19 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_p_full[buf]);
         }
-        // epilogue: O / l -> global
+        // epilogue: O / l -> global (or, for a chunk of a split global row, the
+        // chunk's unnormalised O with its m and l -> partial, merged by the last chunk)
         const uint32_t gl = g + w.n - 1;
         if (!warp_wait(bar_o_done, gl & 1, abort_flag, p.timeout)) return;
         tc_fence_after();
-        const float inv = 1.f / l;
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
         T* orow = reinterpret_cast<T*>(p.out) + (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh +
                   (int64_t)(w.qrow0 + r) * p.o_sn;
         const bool vec = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
-#pragma unroll
-        for (int c = 0; c < D / 32; c++) {
-            uint32_t o[32];
-            tmem_ld32(t_lane + C::O_COL + 32 * c, o);
+        auto store_row = [&](int c, const float* vals) {  // 32 output columns from 32 fp32 values
             uint32_t packed[16];
 #pragma unroll
-            for (int i = 0; i < 16; i++)
-                packed[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+            for (int i = 0; i < 16; i++) packed[i] = pack2<BF16>(vals[2 * i], vals[2 * i + 1]);
             if (vec) {
                 uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
 #pragma unroll
@@ -455,10 +479,89 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                     dst[2 * i + 1] = (uint16_t)(packed[i] >> 16);
                 }
             }
+        };
+        if (!w.split) {
+            const float inv = 1.f / l;
+#pragma unroll
+            for (int c = 0; c < D / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(t_lane + C::O_COL + 32 * c, o);
+                float vals[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) vals[i] = __uint_as_float(o[i]) * inv;
+                store_row(c, vals);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_o_empty);
+        } else {
+            constexpr int PSTRIDE = 128 * D + 256;
+            float* rec = p.partial + ((int64_t)w.group * p.n_chunks + w.chunk) * PSTRIDE;
+#pragma unroll
+            for (int c = 0; c < D / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(t_lane + C::O_COL + 32 * c, o);
+                float4* dst = reinterpret_cast<float4*>(rec + r * D + 32 * c);
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    dst[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                         __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+            }
+            rec[128 * D + r] = m;
+            rec[128 * D + 128 + r] = l;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_o_empty);  // O's TMEM may be reused now
+            __threadfence();                          // partial visible before the count below
+            // all 128 rows written -> count this chunk; the last chunk of the row merges
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_wg);
+            if (!warp_wait(bar_wg, wg_uses & 1, abort_flag, p.timeout)) return;
+            wg_uses++;
+            if (r == 0) {
+                const int done = atomicAdd(&p.chunk_cnt[w.group], 1);
+                const int last = done == p.n_chunks - 1;
+                if (last) p.chunk_cnt[w.group] = 0;  // ready for the next launch
+                *wg_flag = last;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_wg);
+            if (!warp_wait(bar_wg, wg_uses & 1, abort_flag, p.timeout)) return;
+            wg_uses++;
+            if (*wg_flag) {
+                __threadfence();
+                const float* base = p.partial + (int64_t)w.group * p.n_chunks * PSTRIDE;
+                float wt[MAX_CHUNKS];
+                float mmax = -INFINITY;
+                for (int c = 0; c < p.n_chunks; c++) mmax = fmaxf(mmax, __ldcg(base + c * PSTRIDE + 128 * D + r));
+                float lsum = 0.f;
+                for (int c = 0; c < p.n_chunks; c++) {
+                    const float mc = __ldcg(base + c * PSTRIDE + 128 * D + r);
+                    wt[c] = mc == -INFINITY ? 0.f : ex2(mc - mmax);
+                    lsum += wt[c] * __ldcg(base + c * PSTRIDE + 128 * D + 128 + r);
+                }
+                const float inv = 1.f / lsum;
+                for (int c = 0; c < D / 32; c++) {
+                    float vals[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) vals[i] = 0.f;
+                    for (int k = 0; k < p.n_chunks; k++) {
+                        const float4* src = reinterpret_cast<const float4*>(base + k * PSTRIDE + r * D + 32 * c);
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float4 v4 = __ldcg(src + i);
+                            vals[4 * i] += wt[k] * v4.x;
+                            vals[4 * i + 1] += wt[k] * v4.y;
+                            vals[4 * i + 2] += wt[k] * v4.z;
+                            vals[4 * i + 3] += wt[k] * v4.w;
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 32; i++) vals[i] *= inv;
+                    store_row(c, vals);
+                }
+            }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_o_empty);
         g += w.n;
     }
 }
@@ -478,6 +581,8 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
     __shared__ int item_slot[2];
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
+    __shared__ __align__(8) uint64_t bar_wg;
+    __shared__ int wg_flag;
     volatile int* abort_flag = &abort_sh;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -487,6 +592,7 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
         mbar_init(&bar_o_done, 1);
         mbar_init(&bar_o_empty, 4);
         mbar_init(&bar_drain, 1);
+        mbar_init(&bar_wg, 4);
         for (int i = 0; i < C::KS; i++) {
             mbar_init(&bar_k_full[i], 1);
             mbar_init(&bar_k_empty[i], 1);
@@ -531,7 +637,7 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
                                 &bar_o_done, &bar_o_empty, &bar_drain, abort_flag);
     } else if (warp >= 4) {
         softmax_role<D, BF16>(p, tmem, bar_item_full, bar_item_empty, item_slot, bar_s_full, bar_p_full, &bar_o_done,
-                              &bar_o_empty, abort_flag);
+                              &bar_o_empty, &bar_wg, &wg_flag, abort_flag);
     }
     tc_fence_before();
     __syncthreads();
@@ -645,13 +751,46 @@ int launch(const FwdParams& p, int dev, cudaStream_t st) {
 
 using namespace hb;
 
+namespace hb {
+namespace {
+// How the global pair-rows split over their key blocks: chunks of ~CHUNK_BLOCKS
+// blocks (at most MAX_CHUNKS), and the workspace bytes that split needs.
+struct SplitPlan {
+    int chunk, n_chunks;
+    int64_t partial_offset, bytes;
+};
+SplitPlan split_plan(int B, int H, int N, int G, int D) {
+    SplitPlan s;
+    const int nkb = N / 64;
+    s.chunk = std::max(CHUNK_BLOCKS, (nkb + MAX_CHUNKS - 1) / MAX_CHUNKS);
+    s.n_chunks = (nkb + s.chunk - 1) / s.chunk;
+    const int64_t groups = (int64_t)B * H * (G / 128);
+    s.partial_offset = WS_HEADER + ((groups * 4 + 255) / 256) * 256;
+    s.bytes = s.partial_offset + groups * s.n_chunks * (int64_t)(128 * D + 256) * 4;
+    if (groups == 0 || s.n_chunks <= 1) {
+        s.n_chunks = 1;
+        s.chunk = nkb;
+        s.bytes = WS_HEADER;
+    }
+    return s;
+}
+}  // namespace
+}  // namespace hb
+
 extern "C" size_t hb_fwd_workspace_bytes(void) { return 64; }
+
+extern "C" size_t hb_fwd_workspace_bytes_for(int B, int H, int N, int G, int D) {
+    if (B <= 0 || H <= 0 || N <= 0 || N % 128 || G < 0 || G % 128 || G >= N || (D != 64 && D != 128)) return 0;
+    return (size_t)std::max<int64_t>(WS_HEADER, split_plan(B, H, N, G, D).bytes);
+}
 
 extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides, int B,
                              int H, int N, int D, int G, int W, int key_block_size, const int32_t* kv_indices,
                              const int32_t* kv_flags, const int32_t* kv_counts, float scale_log2, int dtype,
-                             void* workspace, void* stream_) {
+                             void* workspace, size_t workspace_bytes, void* stream_) {
     if (!q || !k || !v || !out || !strides || !workspace) return HB_ERR_ARG;
+    if (workspace_bytes < hb_fwd_workspace_bytes() || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return HB_ERR_WORKSPACE;
     if (B <= 0 || H <= 0 || N <= 0 || N % 128 || G < 0 || G % 128 || G >= N || W < 1) return HB_ERR_ARG;
     if (D != 64 && D != 128) return HB_ERR_UNSUPPORTED;
     if (key_block_size != 64) return HB_ERR_UNSUPPORTED;
@@ -687,9 +826,28 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
     p.W = W;
     p.g_rows = G / 128;
     p.o_rows = o_rows;
-    p.n_global_items = B * H * p.g_rows;
-    p.num_items = (int)items;
     p.nkb = N / 64;
+    // Split the global pair-rows (every key block) only when one of them would
+    // outlast a CTA's share of the work (est. from the metadata width W; two CTAs
+    // per SM), and only when the caller's workspace holds the partials.
+    const SplitPlan sp = split_plan(B, H, N, G, D);
+    int n_chunks = 1;
+    if (sp.n_chunks > 1 && workspace_bytes >= (size_t)sp.bytes) {
+        int sms = 0;
+        HB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        const double share = (double)B * H * ((double)p.g_rows * p.nkb + (double)o_rows * W) / (2.0 * sms);
+        const int target = std::max(CHUNK_BLOCKS, (int)(0.75 * share));
+        n_chunks = std::min(sp.n_chunks, (p.nkb + target - 1) / target);
+    }
+    const bool split = n_chunks > 1;
+    p.n_chunks = n_chunks;
+    p.chunk = (p.nkb + n_chunks - 1) / n_chunks;
+    if (split) {
+        p.chunk_cnt = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) + WS_HEADER);
+        p.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + sp.partial_offset);
+    }
+    p.n_global_items = B * H * p.g_rows * p.n_chunks;
+    p.num_items = (int)(items - (int64_t)B * H * p.g_rows + p.n_global_items);
     p.scale_log2 = scale_log2;
     p.timeout = 2000000000ll;
     cudaStream_t st = (cudaStream_t)stream_;
@@ -742,6 +900,7 @@ extern "C" int hb_paired_fwd_noalloc(const void* q, const void* k, const void* v
     // The work counter and finished-CTA counter must start at zero; the array
     // keeps whatever the previous call left, so clear it on the call's stream.
     HB_CUDA_TRY(cudaMemsetAsync(scratch, 0, hb_fwd_workspace_bytes(), (cudaStream_t)stream));
+    // The array holds only the scheduler words, so long global rows run unsplit here.
     return hb_paired_fwd(q, k, v, out, strides, B, H, N, D, G, W, key_block_size, kv_indices, kv_flags, kv_counts,
-                         scale_log2, dtype, scratch, stream);
+                         scale_log2, dtype, scratch, HB_NOALLOC_SCRATCH_BYTES, stream);
 }

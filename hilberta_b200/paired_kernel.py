@@ -24,12 +24,15 @@ LOG2E = 1.4426950408889634
 _workspaces: dict = {}
 
 
-def _workspace(device: torch.device, stream_handle: int) -> torch.Tensor:
-    """Per-(device, stream) scheduler words: zeroed once, self-resetting after."""
+def _workspace(device: torch.device, stream_handle: int, nbytes: int) -> torch.Tensor:
+    """Per-(device, stream) scheduler words and split-row partials: zeroed when
+    (re)allocated, self-resetting after; grown when a call needs more."""
     key = (device.index, stream_handle)
     ws = _workspaces.get(key)
-    if ws is None:
-        n = max(16, _lib.lib().hb_fwd_workspace_bytes() // 4)
+    if ws is None or ws.numel() * 4 < nbytes:
+        n = max(64, -(-max(nbytes, _lib.lib().hb_fwd_workspace_bytes()) // 4))
+        if ws is not None:
+            torch.cuda.current_stream(device).synchronize()  # the old buffer may still be in use
         with torch.inference_mode(False):  # a normal tensor: device_status clears it in place
             ws = torch.zeros(n, dtype=torch.int32, device=device)
         _workspaces[key] = ws
@@ -52,14 +55,15 @@ def _launch(q, k, v, out, metadata, N, G, scale):
     """The one native call of the attention path."""
     dev = q.device
     stream = torch.cuda.current_stream(dev)
-    ws = _workspace(dev, stream.cuda_stream)
-    strides = (ctypes.c_int64 * 12)(*q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *out.stride()[:3])
     B, H, _, D = q.shape
-    rc = _lib.lib().hb_paired_fwd(
+    lib = _lib.lib()
+    ws = _workspace(dev, stream.cuda_stream, lib.hb_fwd_workspace_bytes_for(B, H, N, G, D))
+    strides = (ctypes.c_int64 * 12)(*q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *out.stride()[:3])
+    rc = lib.hb_paired_fwd(
         _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), strides, B, H, N, D, G,
         int(metadata.kv_indices.shape[1]), int(metadata.key_block_size),
         _lib.ptr(metadata.kv_indices), _lib.ptr(metadata.kv_flags), _lib.ptr(metadata.kv_counts),
-        float(scale * LOG2E), 1 if q.dtype == torch.bfloat16 else 0, _lib.ptr(ws),
+        float(scale * LOG2E), 1 if q.dtype == torch.bfloat16 else 0, _lib.ptr(ws), ws.numel() * 4,
         ctypes.c_void_p(stream.cuda_stream),
     )
     if rc == _lib.HB_ERR_TMA:

@@ -126,6 +126,14 @@ int hb_dense_mask(const int32_t* kv_indices, int64_t ld, const int32_t* kv_count
  * different workspaces. */
 size_t hb_fwd_workspace_bytes(void);
 
+/* Workspace bytes with which hb_paired_fwd splits the global pair-rows (every
+ * key block) into chunks of ~32 key blocks that run on different SMs and are
+ * merged by the last chunk (fp32 O/m/l partials + one counter per global
+ * pair-row); 0 for an invalid shape.  A smaller workspace (at least
+ * hb_fwd_workspace_bytes()) runs those rows unsplit.  Zero it once, like the
+ * minimal workspace; the kernel leaves the counters at zero. */
+size_t hb_fwd_workspace_bytes_for(int B, int H, int N, int G, int D);
+
 /* O = softmax(Q K^T * scale | mask) V over the paired metadata, one launch.
  *   q,k,v,out : [B][H][N][D] with element strides strides[t*3 + {0,1,2}] = (b,h,n)
  *               for t = 0 q, 1 k, 2 v, 3 out; the D stride is 1.
@@ -139,7 +147,8 @@ size_t hb_fwd_workspace_bytes(void);
 int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides,
                   int B, int H, int N, int D, int G, int W, int key_block_size,
                   const int32_t* kv_indices, const int32_t* kv_flags, const int32_t* kv_counts,
-                  float scale_log2, int dtype, void* workspace, void* stream);
+                  float scale_log2, int dtype, void* workspace, size_t workspace_bytes,
+                  void* stream);
 
 /* ---- allocation-free variant of hb_paired_fwd --------------------------- */
 /* No counterpart in the reference: an addition for callers that must not

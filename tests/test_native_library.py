@@ -38,6 +38,11 @@ def test_status_strings(lib):
     assert "Shared square" in _lib.status_text(_lib.HB_ERR_SHARED)
     assert lib.hb_version() >= 100
     assert lib.hb_fwd_workspace_bytes() >= 12
+    # 2048^2 t16k3 shape: 24 heads x 4 global pair-rows split into 9 chunks of fp32 partials
+    big = lib.hb_fwd_workspace_bytes_for(1, 24, 16896, 512, 128)
+    assert big > 24 * 4 * 9 * 128 * 128 * 4
+    assert lib.hb_fwd_workspace_bytes_for(1, 24, 16896, 0, 128) == 256  # no global rows: nothing to split
+    assert lib.hb_fwd_workspace_bytes_for(1, 24, 16896, 100, 128) == 0
 
 
 def test_plan_dims_preconditions(lib):
@@ -57,14 +62,17 @@ def test_invalid_arguments_rejected_before_any_launch(lib):
     from hilberta_b200 import _lib
 
     null = None
-    assert lib.hb_paired_fwd(null, null, null, null, null, 1, 1, 256, 128, 0, 1, 64, null, null, null, 1.0, 1, null, null) == _lib.HB_ERR_ARG
+    assert lib.hb_paired_fwd(null, null, null, null, null, 1, 1, 256, 128, 0, 1, 64, null, null, null, 1.0, 1, null, 0, null) == _lib.HB_ERR_ARG
     strides = (ctypes.c_int64 * 12)(*([1] * 12))
     fake = ctypes.c_void_p(1 << 20)
     # D = 96 unsupported, key block 128 unsupported, N not a multiple of 128
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 96, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, null) == _lib.HB_ERR_UNSUPPORTED
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 128, fake, fake, fake, 1.0, 1, fake, null) == _lib.HB_ERR_UNSUPPORTED
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 200, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, null) == _lib.HB_ERR_ARG
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 256, 1, 64, fake, fake, fake, 1.0, 1, fake, null) == _lib.HB_ERR_ARG
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 96, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, 256, null) == _lib.HB_ERR_UNSUPPORTED
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 128, fake, fake, fake, 1.0, 1, fake, 256, null) == _lib.HB_ERR_UNSUPPORTED
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 200, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, 256, null) == _lib.HB_ERR_ARG
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 256, 1, 64, fake, fake, fake, 1.0, 1, fake, 256, null) == _lib.HB_ERR_ARG
+    # workspace below the minimum / misaligned
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, 16, null) == _lib.HB_ERR_WORKSPACE
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, ctypes.c_void_p((1 << 20) + 64), 256, null) == _lib.HB_ERR_WORKSPACE
     assert lib.hb_pair_metadata(fake, 4, fake, 3, 512, 128, 64, fake, fake, 8, fake, fake, null) == _lib.HB_ERR_ARG
     assert lib.hb_validate_metadata(fake, 2, 4, fake, 3, 512, 128, fake, null) == _lib.HB_ERR_ARG
 

@@ -38,7 +38,8 @@ def test_noalloc_matches_allocating_entry_on_two_calls():
     plan = hb.bridge_k_plan(16, 3, False, grid_size=64)
     N, G = plan.total_tokens, plan.global_tokens
     stream = torch.cuda.current_stream(dev).cuda_stream
-    workspace = torch.zeros(max(16, lib.hb_fwd_workspace_bytes() // 4), dtype=torch.int32, device=dev)
+    ws_bytes = lib.hb_fwd_workspace_bytes_for(1, 4, N, G, 128)
+    workspace = torch.zeros(ws_bytes // 4, dtype=torch.int32, device=dev)
     scale_log2 = 128**-0.5 * 1.4426950408889634
     for call, phase in enumerate((1, 3)):  # two calls in a row, different inputs and metadata
         p = plan.phases[phase]
@@ -49,7 +50,7 @@ def test_noalloc_matches_allocating_entry_on_two_calls():
         args = (meta.kv_indices.shape[1], 64, _lib.ptr(meta.kv_indices), _lib.ptr(meta.kv_flags), _lib.ptr(meta.kv_counts))
         rc = lib.hb_paired_fwd(
             _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(ref), _strides(q, k, v, ref), 1, 4, N, 128, G, *args,
-            scale_log2, 1, _lib.ptr(workspace), ctypes.c_void_p(stream),
+            scale_log2, 1, _lib.ptr(workspace), ws_bytes, ctypes.c_void_p(stream),
         )
         assert rc == 0, _lib.status_text(rc)
         rc = lib.hb_paired_fwd_noalloc(
