@@ -78,7 +78,7 @@ _SIGS = {
     "hb_paired_fwd": (
         _I,
         [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P,
-         ctypes.c_size_t, _P],
+         _P, ctypes.c_size_t, _P],
     ),
     "hb_paired_fwd_noalloc": (
         _I,

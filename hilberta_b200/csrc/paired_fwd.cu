@@ -64,15 +64,25 @@ struct FwdParams {
     int chunk, n_chunks;
     float* partial;      // [B*H*g_rows][n_chunks][128*D + 256] fp32
     int32_t* chunk_cnt;  // [B*H*g_rows] finished chunks (reset to 0 by the merger)
+    // Fused token permutation: physical token p of the layout the metadata indexes
+    // reads and writes source row row_map[p] of Q/K/V/O (null: identity).  The
+    // gathered tensor maps are 2-D (D, rows); rs_* = (b, h, n) strides in rows.
+    const int32_t* row_map;
+    int64_t rs_q[3], rs_k[3], rs_v[3];
     float scale_log2;
     long long timeout;  // SM cycles a single barrier wait may take
 };
 
 // Scratch layout of the workspace, in bytes: header (scheduler words), chunk
-// counters, then the chunk partials.
+// counters, then the chunk partials.  The counter region's size depends only on
+// the workspace size (room for every group a split launch could fit), so the
+// partials of one launch never overlap the counters of a launch with more groups
+// that uses the same workspace: the counters stay zero between launches.
 constexpr int64_t WS_HEADER = 256;
 constexpr int MAX_CHUNKS = 32;
-constexpr int CHUNK_BLOCKS = 32;  // target key blocks per chunk of a global pair-row
+constexpr int CHUNK_BLOCKS = 32;                          // target key blocks per chunk of a global pair-row
+constexpr int64_t MIN_GROUP_PARTIAL = 2 * (128 * 64 + 256) * 4;  // smallest partials of one split group
+inline int64_t counter_bytes(int64_t ws) { return ((4 * (ws / MIN_GROUP_PARTIAL + 1) + 255) / 256) * 256; }
 
 template <int D>
 struct Cfg {
@@ -182,8 +192,28 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     }
 }
 
-// Producer of one operand stream (warp-wide; lane 0 issues).  WHICH = 0: Q + K, 1: V.
-template <int D, int WHICH>
+// Gather mode: lane i (i < rows/4) loads token rows base+4i..base+4i+3 of a tile
+// through the physical -> source row map, one tile::gather4 per 64-column slab
+// into 128-byte rows 4i..4i+3 of the tile (the same swizzled layout a tiled load
+// gives).  rs = (b, h, n) strides of the tensor in rows of D elements.
+template <int D>
+__device__ __forceinline__ void gather_tile(const FwdParams& p, const CUtensorMap* map, const int64_t* rs, uint8_t* dst,
+                                            int slab_bytes, uint64_t* bar, int base, int rows, int b, int h, bool bad) {
+    const int lane = threadIdx.x & 31;
+    if (4 * lane >= rows) return;
+    const int4 src = *reinterpret_cast<const int4*>(p.row_map + base + 4 * lane);
+    const int64_t r0 = (int64_t)b * rs[0] + (int64_t)h * rs[1];
+    const int s0 = bad ? -1 : (int)(r0 + (int64_t)src.x * rs[2]);
+    const int s1 = bad ? -1 : (int)(r0 + (int64_t)src.y * rs[2]);
+    const int s2 = bad ? -1 : (int)(r0 + (int64_t)src.z * rs[2]);
+    const int s3 = bad ? -1 : (int)(r0 + (int64_t)src.w * rs[2]);
+#pragma unroll
+    for (int s = 0; s < D / 64; s++) tma_gather4(dst + s * slab_bytes + 4 * lane * 128, map, bar, 64 * s, s0, s1, s2, s3);
+}
+
+// Producer of one operand stream (warp-wide; lane 0 issues, every lane in gather
+// mode).  WHICH = 0: Q + K, 1: V.
+template <int D, int WHICH, bool GATHER>
 __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t* bar_item_full,
                          uint64_t* bar_item_empty, int* item_slot, uint64_t* bar_q_full, uint64_t* bar_q_empty,
                          uint64_t* bar_full, uint64_t* bar_empty, volatile int* abort_flag) {
@@ -192,6 +222,7 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
     const int lane = threadIdx.x & 31;
     const CUtensorMap* tmap = WHICH == 0 ? &p.tmap_k : &p.tmap_v;
     const int32_t* perm = WHICH == 0 ? p.perm_k : p.perm_v;
+    const int64_t* rs = WHICH == 0 ? p.rs_k : p.rs_v;
     uint32_t gx = 0;  // loads issued over this CTA's lifetime
     bool ok = true;
     for (int it = 0; ok; it++) {
@@ -216,7 +247,11 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
         const Item w = decode_item(p, item, WHICH == 0 && lane == 0);
         if (WHICH == 0) {
             if (!warp_wait(bar_q_empty, (it & 1) ^ 1, abort_flag, p.timeout)) break;
-            if (lane == 0) {
+            if constexpr (GATHER) {
+                if (lane == 0) mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
+                __syncwarp();
+                gather_tile<D>(p, &p.tmap_q, p.rs_q, sQ, C::Q_SLAB, bar_q_full, w.qrow0, 128, w.b, w.h, false);
+            } else if (lane == 0) {
                 mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
                 int c1, c2, c3;
                 tma_coords(p.perm_q, w.qrow0, w.h, w.b, c1, c2, c3);
@@ -236,9 +271,19 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
                 ok = false;
                 break;
             }
-            if (lane == 0) {
+            const bool bad = blk < 0 || blk >= p.nkb;
+            if constexpr (GATHER) {
+                if (lane == 0) {
+                    if (bad) atomicOr(&p.ws[2], HB_DEV_BAD_BLOCK);
+                    mbar_arrive_expect_tx(&bar_full[st], C::KV_BYTES);
+                }
+                __syncwarp();
+                // a bad block reads row -1: out of bounds, the TMA unit fills zeros
+                gather_tile<D>(p, tmap, rs, sKV + st * C::KV_BYTES, C::KV_SLAB, &bar_full[st], bad ? 0 : blk * 64, 64,
+                               w.b, w.h, bad);
+            } else if (lane == 0) {
                 int rowc = blk * 64;
-                if (blk < 0 || blk >= p.nkb) {
+                if (bad) {
                     rowc = p.N;  // fully out of bounds: the TMA unit fills zeros
                     atomicOr(&p.ws[2], HB_DEV_BAD_BLOCK);
                 }
@@ -460,7 +505,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
         tc_fence_after();
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
         T* orow = reinterpret_cast<T*>(p.out) + (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh +
-                  (int64_t)(w.qrow0 + r) * p.o_sn;
+                  (int64_t)(p.row_map ? p.row_map[w.qrow0 + r] : w.qrow0 + r) * p.o_sn;
         const bool vec = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
         auto store_row = [&](int c, const float* vals) {  // 32 output columns from 32 fp32 values
             uint32_t packed[16];
@@ -566,7 +611,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
     }
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool GATHER>
 __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ FwdParams p) {
     using C = Cfg<D>;
     extern __shared__ uint8_t smem_raw[];
@@ -625,10 +670,10 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
     const uint32_t tmem = tmem_base_sh;
 
     if (warp == 0) {
-        producer<D, 0>(p, sQ, sK, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_k_full,
+        producer<D, 0, GATHER>(p, sQ, sK, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_k_full,
                        bar_k_empty, abort_flag);
     } else if (warp == 1) {
-        producer<D, 1>(p, sQ, sV, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_v_full,
+        producer<D, 1, GATHER>(p, sQ, sV, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_v_full,
                        bar_v_empty, abort_flag);
     } else if (warp == 2) {
         if (lane == 0)
@@ -717,18 +762,48 @@ int make_tmap(CUtensorMap* map, const void* base, bool bf16, int D, int N, int H
     return r == CUDA_SUCCESS ? HB_OK : HB_ERR_TMA;
 }
 
+// Gather mode: the tensor as 2-D (D, rows) with a one-row box, where row
+// b*rs[0] + h*rs[1] + n*rs[2] holds token n of head h, batch b.  Needs every
+// outer stride to be a multiple of D (rows of D contiguous elements).
+int make_tmap_rows(CUtensorMap* map, const void* base, bool bf16, int D, int N, int H, int B, int64_t sb, int64_t sh,
+                   int64_t sn, int64_t rs[3]) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return HB_ERR_CUDA;
+    if (reinterpret_cast<uintptr_t>(base) & 15) return HB_ERR_TMA;
+    const int64_t ext[3] = {B, H, N}, st[3] = {sb, sh, sn};
+    int64_t rows = 1;
+    for (int i = 0; i < 3; i++) {
+        if (ext[i] == 1) {
+            rs[i] = 0;
+            continue;
+        }
+        if (st[i] <= 0 || st[i] % D) return HB_ERR_TMA;
+        rs[i] = st[i] / D;
+        rows += (ext[i] - 1) * rs[i];
+    }
+    if (rows >= INT32_MAX) return HB_ERR_UNSUPPORTED;
+    cuuint64_t gdim[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)D * 2};
+    cuuint32_t box[2] = {64, 1}, estride[2] = {1, 1};
+    const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                           const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? HB_OK : HB_ERR_TMA;
+}
+
 struct DeviceInfo {
     int sms = 0;
-    bool configured[4] = {false, false, false, false};
+    bool configured[8] = {false, false, false, false, false, false, false, false};
 };
 std::mutex g_mu;
 DeviceInfo g_dev[64];
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool GATHER>
 int launch(const FwdParams& p, int dev, cudaStream_t st) {
     using C = Cfg<D>;
-    auto kern = k_paired_fwd<D, BF16>;
-    const int slot = (D == 128 ? 2 : 0) + (BF16 ? 1 : 0);
+    auto kern = k_paired_fwd<D, BF16, GATHER>;
+    const int slot = (D == 128 ? 2 : 0) + (BF16 ? 1 : 0) + (GATHER ? 4 : 0);
     int sms;
     {
         std::lock_guard<std::mutex> lk(g_mu);
@@ -757,7 +832,7 @@ namespace {
 // blocks (at most MAX_CHUNKS), and the workspace bytes that split needs.
 struct SplitPlan {
     int chunk, n_chunks;
-    int64_t partial_offset, bytes;
+    int64_t partial_bytes, bytes;  // bytes: smallest workspace that fits the partials
 };
 SplitPlan split_plan(int B, int H, int N, int G, int D) {
     SplitPlan s;
@@ -765,14 +840,24 @@ SplitPlan split_plan(int B, int H, int N, int G, int D) {
     s.chunk = std::max(CHUNK_BLOCKS, (nkb + MAX_CHUNKS - 1) / MAX_CHUNKS);
     s.n_chunks = (nkb + s.chunk - 1) / s.chunk;
     const int64_t groups = (int64_t)B * H * (G / 128);
-    s.partial_offset = WS_HEADER + ((groups * 4 + 255) / 256) * 256;
-    s.bytes = s.partial_offset + groups * s.n_chunks * (int64_t)(128 * D + 256) * 4;
+    s.partial_bytes = groups * s.n_chunks * (int64_t)(128 * D + 256) * 4;
     if (groups == 0 || s.n_chunks <= 1) {
         s.n_chunks = 1;
         s.chunk = nkb;
+        s.partial_bytes = 0;
         s.bytes = WS_HEADER;
+        return s;
     }
+    // Smallest size with 256 bytes to spare over header + counters + partials;
+    // the spare keeps every larger size fitting too (the counter region grows
+    // by 256 bytes per ~4 MB of workspace).
+    int64_t w = WS_HEADER + s.partial_bytes;
+    while (w < WS_HEADER + counter_bytes(w) + s.partial_bytes + 256) w = WS_HEADER + counter_bytes(w) + s.partial_bytes + 256;
+    s.bytes = w;
     return s;
+}
+inline bool split_fits(const SplitPlan& s, int64_t ws) {
+    return s.partial_bytes > 0 && ws - WS_HEADER - counter_bytes(ws) >= s.partial_bytes;
 }
 }  // namespace
 }  // namespace hb
@@ -787,8 +872,9 @@ extern "C" size_t hb_fwd_workspace_bytes_for(int B, int H, int N, int G, int D) 
 extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides, int B,
                              int H, int N, int D, int G, int W, int key_block_size, const int32_t* kv_indices,
                              const int32_t* kv_flags, const int32_t* kv_counts, float scale_log2, int dtype,
-                             void* workspace, size_t workspace_bytes, void* stream_) {
+                             const int32_t* row_map, void* workspace, size_t workspace_bytes, void* stream_) {
     if (!q || !k || !v || !out || !strides || !workspace) return HB_ERR_ARG;
+    if (row_map && (reinterpret_cast<uintptr_t>(row_map) & 15)) return HB_ERR_ARG;
     if (workspace_bytes < hb_fwd_workspace_bytes() || (reinterpret_cast<uintptr_t>(workspace) & 255))
         return HB_ERR_WORKSPACE;
     if (B <= 0 || H <= 0 || N <= 0 || N % 128 || G < 0 || G % 128 || G >= N || W < 1) return HB_ERR_ARG;
@@ -808,9 +894,16 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
     memset(&p, 0, sizeof(p));
     const bool bf16 = dtype == 1;
     int rc;
-    if ((rc = make_tmap(&p.tmap_q, q, bf16, D, N, H, B, strides[0], strides[1], strides[2], 128, p.perm_q))) return rc;
-    if ((rc = make_tmap(&p.tmap_k, k, bf16, D, N, H, B, strides[3], strides[4], strides[5], 64, p.perm_k))) return rc;
-    if ((rc = make_tmap(&p.tmap_v, v, bf16, D, N, H, B, strides[6], strides[7], strides[8], 64, p.perm_v))) return rc;
+    if (row_map) {
+        p.row_map = row_map;
+        if ((rc = make_tmap_rows(&p.tmap_q, q, bf16, D, N, H, B, strides[0], strides[1], strides[2], p.rs_q))) return rc;
+        if ((rc = make_tmap_rows(&p.tmap_k, k, bf16, D, N, H, B, strides[3], strides[4], strides[5], p.rs_k))) return rc;
+        if ((rc = make_tmap_rows(&p.tmap_v, v, bf16, D, N, H, B, strides[6], strides[7], strides[8], p.rs_v))) return rc;
+    } else {
+        if ((rc = make_tmap(&p.tmap_q, q, bf16, D, N, H, B, strides[0], strides[1], strides[2], 128, p.perm_q))) return rc;
+        if ((rc = make_tmap(&p.tmap_k, k, bf16, D, N, H, B, strides[3], strides[4], strides[5], 64, p.perm_k))) return rc;
+        if ((rc = make_tmap(&p.tmap_v, v, bf16, D, N, H, B, strides[6], strides[7], strides[8], 64, p.perm_v))) return rc;
+    }
     p.out = out;
     p.o_sb = strides[9];
     p.o_sh = strides[10];
@@ -832,7 +925,7 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
     // per SM), and only when the caller's workspace holds the partials.
     const SplitPlan sp = split_plan(B, H, N, G, D);
     int n_chunks = 1;
-    if (sp.n_chunks > 1 && workspace_bytes >= (size_t)sp.bytes) {
+    if (sp.n_chunks > 1 && split_fits(sp, (int64_t)workspace_bytes)) {
         int sms = 0;
         HB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
         const double share = (double)B * H * ((double)p.g_rows * p.nkb + (double)o_rows * W) / (2.0 * sms);
@@ -844,15 +937,20 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
     p.chunk = (p.nkb + n_chunks - 1) / n_chunks;
     if (split) {
         p.chunk_cnt = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) + WS_HEADER);
-        p.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + sp.partial_offset);
+        p.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + WS_HEADER +
+                                             counter_bytes((int64_t)workspace_bytes));
     }
     p.n_global_items = B * H * p.g_rows * p.n_chunks;
     p.num_items = (int)(items - (int64_t)B * H * p.g_rows + p.n_global_items);
     p.scale_log2 = scale_log2;
     p.timeout = 2000000000ll;
     cudaStream_t st = (cudaStream_t)stream_;
-    if (D == 128) return bf16 ? launch<128, true>(p, dev, st) : launch<128, false>(p, dev, st);
-    return bf16 ? launch<64, true>(p, dev, st) : launch<64, false>(p, dev, st);
+    if (row_map) {
+        if (D == 128) return bf16 ? launch<128, true, true>(p, dev, st) : launch<128, false, true>(p, dev, st);
+        return bf16 ? launch<64, true, true>(p, dev, st) : launch<64, false, true>(p, dev, st);
+    }
+    if (D == 128) return bf16 ? launch<128, true, false>(p, dev, st) : launch<128, false, false>(p, dev, st);
+    return bf16 ? launch<64, true, false>(p, dev, st) : launch<64, false, false>(p, dev, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -902,5 +1000,5 @@ extern "C" int hb_paired_fwd_noalloc(const void* q, const void* k, const void* v
     HB_CUDA_TRY(cudaMemsetAsync(scratch, 0, hb_fwd_workspace_bytes(), (cudaStream_t)stream));
     // The array holds only the scheduler words, so long global rows run unsplit here.
     return hb_paired_fwd(q, k, v, out, strides, B, H, N, D, G, W, key_block_size, kv_indices, kv_flags, kv_counts,
-                         scale_log2, dtype, scratch, HB_NOALLOC_SCRATCH_BYTES, stream);
+                         scale_log2, dtype, nullptr, scratch, HB_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -40,18 +40,22 @@ def _workspace(device: torch.device, stream_handle: int, nbytes: int) -> torch.T
 
 
 def device_status(device=None, *, clear=True) -> int:
-    """OR of the HB_DEV_* bits the kernel reported on `device` (synchronises)."""
+    """OR of the HB_DEV_* bits the kernel reported on `device` (synchronises).
+
+    With ``clear``, resets the status word; a workspace whose launch gave up on a
+    wait (HB_DEV_TIMEOUT) may hold stale scheduler words and is zeroed whole."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     bits = 0
     for (index, _), ws in _workspaces.items():
         if index == dev.index:
-            bits |= int(ws[2].item())
+            word = int(ws[2].item())
+            bits |= word
             if clear:
-                ws[2].zero_()
+                (ws if word & _lib.HB_DEV_TIMEOUT else ws[2]).zero_()
     return bits
 
 
-def _launch(q, k, v, out, metadata, N, G, scale):
+def _launch(q, k, v, out, metadata, N, G, scale, row_map=None):
     """The one native call of the attention path."""
     dev = q.device
     stream = torch.cuda.current_stream(dev)
@@ -63,8 +67,8 @@ def _launch(q, k, v, out, metadata, N, G, scale):
         _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), strides, B, H, N, D, G,
         int(metadata.kv_indices.shape[1]), int(metadata.key_block_size),
         _lib.ptr(metadata.kv_indices), _lib.ptr(metadata.kv_flags), _lib.ptr(metadata.kv_counts),
-        float(scale * LOG2E), 1 if q.dtype == torch.bfloat16 else 0, _lib.ptr(ws), ws.numel() * 4,
-        ctypes.c_void_p(stream.cuda_stream),
+        float(scale * LOG2E), 1 if q.dtype == torch.bfloat16 else 0, _lib.ptr(row_map), _lib.ptr(ws),
+        ws.numel() * 4, ctypes.c_void_p(stream.cuda_stream),
     )
     if rc == _lib.HB_ERR_TMA:
         raise ValueError("Q/K/V need 16-byte aligned base pointers and strides for TMA tiles")
@@ -73,14 +77,29 @@ def _launch(q, k, v, out, metadata, N, G, scale):
     _lib.check(rc, "hb_paired_fwd")
 
 
+def token_order_map(plan, device) -> torch.Tensor:
+    """Physical -> raster row map of a plan for ``paired_attention(token_order=...)``:
+    text rows first (identity), then ``text_tokens + image_order`` (plan.py:147)."""
+    t = int(plan.text_tokens)
+    order = torch.as_tensor(plan.image_order).to(torch.int64)
+    rows = torch.cat([torch.arange(t, dtype=torch.int64), t + order.cpu()])
+    return rows.to(torch.int32).to(device).contiguous()
+
+
 def paired_attention(
-    q, k, v, metadata, *, global_strategy="flash", num_warps=4, num_stages=2, scale=None, out=None
+    q, k, v, metadata, *, global_strategy="flash", num_warps=4, num_stages=2, scale=None, out=None, token_order=None
 ):
     """Exact inference; pair metadata must be validated on CPU before transfer.
 
     Q/K/V ``[B,H,N,D]`` (D 64 or 128, contiguous D, any positive outer strides,
     e.g. BNHD storage viewed as BHND), fp16/bf16.  Returns ``out`` (allocated
     with ``torch.empty_like(q)`` when not given, preserving q's storage order).
+
+    ``token_order`` (extension, keyword only): int32 CUDA tensor [N] mapping each
+    physical token of the metadata's layout to its row in q/k/v/out, e.g.
+    ``token_order_map(plan, device)`` for tensors kept in raster order; the
+    kernel then gathers rows while loading and scatters output rows, replacing
+    the reference's separate reorder pass (sampling_layout.py:88-116).
     """
     if q.ndim != 4 or k.shape != q.shape or v.shape != q.shape or any(x <= 0 for x in q.shape):
         raise ValueError("Equal nonempty B,H,N,D Q/K/V required")
@@ -134,5 +153,16 @@ def paired_attention(
                 raise ValueError("Output cannot alias inputs or metadata")
     else:
         out = torch.empty_like(q)
-    _launch(q, k, v, out, metadata, N, G, scale)
+    if token_order is not None:
+        if (
+            not isinstance(token_order, torch.Tensor)
+            or token_order.dtype != torch.int32
+            or token_order.device != q.device
+            or token_order.shape != (N,)
+            or not token_order.is_contiguous()
+        ):
+            raise ValueError("token_order must be a contiguous int32 [N] tensor on the Q device")
+        if any(s % q.shape[-1] for x in (q, k, v) for s in x.stride()[:3]):
+            raise ValueError("token_order needs Q/K/V outer strides that are multiples of D")
+    _launch(q, k, v, out, metadata, N, G, scale, token_order)
     return out

@@ -129,9 +129,12 @@ size_t hb_fwd_workspace_bytes(void);
 /* Workspace bytes with which hb_paired_fwd splits the global pair-rows (every
  * key block) into chunks of ~32 key blocks that run on different SMs and are
  * merged by the last chunk (fp32 O/m/l partials + one counter per global
- * pair-row); 0 for an invalid shape.  A smaller workspace (at least
- * hb_fwd_workspace_bytes()) runs those rows unsplit.  Zero it once, like the
- * minimal workspace; the kernel leaves the counters at zero. */
+ * pair-row); 0 for an invalid shape.  Any larger workspace splits too; a
+ * smaller one (at least hb_fwd_workspace_bytes()) runs those rows unsplit.
+ * Zero it once, like the minimal workspace; the kernel leaves the counters at
+ * zero.  The counters sit in a region sized by workspace_bytes alone, so one
+ * workspace serves launches of any shape as long as every launch passes the
+ * same workspace_bytes for it.  After HB_DEV_TIMEOUT, zero it again. */
 size_t hb_fwd_workspace_bytes_for(int B, int H, int N, int G, int D);
 
 /* O = softmax(Q K^T * scale | mask) V over the paired metadata, one launch.
@@ -147,8 +150,17 @@ size_t hb_fwd_workspace_bytes_for(int B, int H, int N, int G, int D);
 int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides,
                   int B, int H, int N, int D, int G, int W, int key_block_size,
                   const int32_t* kv_indices, const int32_t* kv_flags, const int32_t* kv_counts,
-                  float scale_log2, int dtype, void* workspace, size_t workspace_bytes,
-                  void* stream);
+                  float scale_log2, int dtype, const int32_t* row_map, void* workspace,
+                  size_t workspace_bytes, void* stream);
+/* row_map (optional, NULL = identity; device int32 [N], 16-byte aligned): fused
+ * token permutation.  Physical token p — the order the metadata indexes (text
+ * prefix, then image tokens in Hilbert / packed order) — is read from row
+ * row_map[p] of Q, K and V and written to row row_map[p] of out, so callers can
+ * keep Q/K/V/O in raster token order (row_map = [0..T) ++ T + image_order,
+ * hilberta/plan.py:147) and no separate reorder pass
+ * (hilberta/sampling_layout.py:88-116) touches HBM.  Rows are gathered with TMA
+ * tile::gather4 (4 rows per instruction); Q/K/V outer strides must then be
+ * multiples of D. */
 
 /* ---- allocation-free variant of hb_paired_fwd --------------------------- */
 /* No counterpart in the reference: an addition for callers that must not

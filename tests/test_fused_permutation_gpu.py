@@ -1,0 +1,76 @@
+"""Fused Hilbert gather/scatter (``paired_attention(token_order=...)``): with Q/K/V
+kept in raster token order, the kernel gathers rows through the plan's
+physical -> raster map while loading and scatters output rows, so the result
+must equal permuting the inputs (``index_select``, the reference's entry pass,
+hilberta/sampling_layout.py:88-103), running the kernel on the physical layout
+and inverting the permutation (sampling_layout.py:105-113) — bit for bit, since
+both run the same tiles in the same order."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import attention_oracle as ao
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(tiles, k, grid, heads, layout, phase, seed):
+    import hilberta_b200 as hb
+    from hilberta_b200.paired_kernel import token_order_map
+
+    dev = torch.device("cuda", 0)
+    plan = hb.bridge_k_plan(tiles, k, False, grid_size=grid)
+    N, G = plan.total_tokens, plan.global_tokens
+    p = plan.phases[phase]
+    meta = hb.pair_metadata(p.kv_indices, p.kv_counts, tokens=N, global_tokens=G).to(dev)
+    rows = token_order_map(plan, dev)
+    q, kk, v = (x.to(dev) for x in ao.seeded_qkv(1, heads, N, 128, seed=seed, layout=layout))  # raster order
+    kw = dict(global_strategy="triton", num_warps=8, num_stages=2)
+    with torch.inference_mode():
+        fused = hb.paired_attention(q, kk, v, meta, token_order=rows, **kw)
+        idx = rows.long()
+        phys = [x.index_select(2, idx) for x in (q, kk, v)]
+        out_phys = hb.paired_attention(*phys, meta, **kw)
+        unperm = torch.empty_like(out_phys)
+        unperm[:, :, idx] = out_phys
+    torch.cuda.synchronize()
+    assert hb.device_status() == 0
+    return fused, unperm, (q, kk, v, p, N, G, rows)
+
+
+@pytest.mark.parametrize("layout", ["bhnd", "bnhd"])
+def test_fused_permutation_equals_explicit_reorder(layout):
+    fused, ref, _ = _case(4, 1, 32, 2, layout, 1, 51)
+    assert torch.equal(fused, ref)
+
+
+def test_fused_permutation_against_oracle():
+    fused, _, (q, k, v, p, N, G, rows) = _case(16, 3, 64, 3, "bnhd", 2, 52)
+    # oracle in the physical layout, then scattered back to raster rows
+    idx = rows.long().cpu()
+    phys = [x.cpu().index_select(2, idx) for x in (q, k, v)]
+    ref_phys = ao.masked_attention_fp32(*phys, ao.block_mask_from_rows(p.kv_indices, p.kv_counts, N, G))
+    ref = torch.empty_like(ref_phys)
+    ref[:, :, idx] = ref_phys
+    err = (fused.float().cpu() - ref).abs()
+    assert float(err.max()) <= 2e-2 and float(err.mean()) <= 2e-3
+
+
+def test_fused_permutation_2048_t16k3_all_heads():
+    fused, ref, _ = _case(16, 3, 128, 24, "bnhd", 0, 53)
+    assert torch.equal(fused, ref)
+
+
+def test_token_order_validation():
+    import hilberta_b200 as hb
+
+    dev = torch.device("cuda", 0)
+    plan = hb.bridge_k_plan(4, 1, False, grid_size=32)
+    N, G = plan.total_tokens, plan.global_tokens
+    p = plan.phases[0]
+    meta = hb.pair_metadata(p.kv_indices, p.kv_counts, tokens=N, global_tokens=G).to(dev)
+    q = torch.zeros(1, 2, N, 128, dtype=torch.bfloat16, device=dev)
+    with pytest.raises(ValueError, match="token_order"):
+        hb.paired_attention(q, q.clone(), q.clone(), meta, token_order=torch.arange(N, device=dev))  # int64

@@ -62,17 +62,17 @@ def test_invalid_arguments_rejected_before_any_launch(lib):
     from hilberta_b200 import _lib
 
     null = None
-    assert lib.hb_paired_fwd(null, null, null, null, null, 1, 1, 256, 128, 0, 1, 64, null, null, null, 1.0, 1, null, 0, null) == _lib.HB_ERR_ARG
+    assert lib.hb_paired_fwd(null, null, null, null, null, 1, 1, 256, 128, 0, 1, 64, null, null, null, 1.0, 1, null, null, 0, null) == _lib.HB_ERR_ARG
     strides = (ctypes.c_int64 * 12)(*([1] * 12))
     fake = ctypes.c_void_p(1 << 20)
     # D = 96 unsupported, key block 128 unsupported, N not a multiple of 128
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 96, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, 256, null) == _lib.HB_ERR_UNSUPPORTED
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 128, fake, fake, fake, 1.0, 1, fake, 256, null) == _lib.HB_ERR_UNSUPPORTED
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 200, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, 256, null) == _lib.HB_ERR_ARG
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 256, 1, 64, fake, fake, fake, 1.0, 1, fake, 256, null) == _lib.HB_ERR_ARG
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 96, 0, 1, 64, fake, fake, fake, 1.0, 1, null, fake, 256, null) == _lib.HB_ERR_UNSUPPORTED
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 128, fake, fake, fake, 1.0, 1, null, fake, 256, null) == _lib.HB_ERR_UNSUPPORTED
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 200, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, null, fake, 256, null) == _lib.HB_ERR_ARG
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 256, 1, 64, fake, fake, fake, 1.0, 1, null, fake, 256, null) == _lib.HB_ERR_ARG
     # workspace below the minimum / misaligned
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, fake, 16, null) == _lib.HB_ERR_WORKSPACE
-    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, ctypes.c_void_p((1 << 20) + 64), 256, null) == _lib.HB_ERR_WORKSPACE
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, null, fake, 16, null) == _lib.HB_ERR_WORKSPACE
+    assert lib.hb_paired_fwd(fake, fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, null, ctypes.c_void_p((1 << 20) + 64), 256, null) == _lib.HB_ERR_WORKSPACE
     assert lib.hb_pair_metadata(fake, 4, fake, 3, 512, 128, 64, fake, fake, 8, fake, fake, null) == _lib.HB_ERR_ARG
     assert lib.hb_validate_metadata(fake, 2, 4, fake, 3, 512, 128, fake, null) == _lib.HB_ERR_ARG
 

@@ -205,3 +205,23 @@ def test_repeated_calls_bitwise_deterministic():
     a = _run(q, k, v, meta)
     b = _run(q, k, v, meta)
     assert torch.equal(a, b)
+
+
+def test_shared_workspace_across_split_shapes():
+    """One workspace serving split launches of different group counts: the
+    partials of a launch with few groups must not leave words where a launch with
+    more groups keeps its chunk counters (result equals a fresh workspace's)."""
+    import hilberta_b200 as hb
+    from hilberta_b200 import paired_kernel as pk
+
+    plan64 = hb.bridge_k_plan(16, 3, False, grid_size=64)
+    meta64, _ = _meta(plan64, 2)
+    q, k, v = (x.cuda() for x in ao.seeded_qkv(1, 24, plan64.total_tokens, 128, seed=7))
+    pk._workspaces.clear()
+    fresh = _run(q, k, v, meta64)
+    plan128 = hb.bridge_k_plan(16, 3, False, grid_size=128)  # grows the workspace
+    meta128, _ = _meta(plan128, 0)
+    _run(*(x.cuda() for x in ao.seeded_qkv(1, 24, plan128.total_tokens, 128, seed=8)), meta128)
+    _run(q[:, :2], k[:, :2], v[:, :2], meta64)  # few groups: partials right after the counters
+    assert torch.equal(_run(q, k, v, meta64), fresh)
+    assert torch.equal(_run(q, k, v, meta64), fresh)

@@ -78,7 +78,7 @@ class PairedContract(unittest.TestCase):
     def test_mixed_stride_native_output(self):
         self.assertIs(self.call(), self.out)
         args = self.last_launch.call_args[0]
-        self.assertEqual(args[5:], (512, 128, 128**-0.5))
+        self.assertEqual(args[5:8], (512, 128, 128**-0.5))
 
     def test_flash_strategy_uses_the_same_single_launch(self):
         launch = MagicMock()

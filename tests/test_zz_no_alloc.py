@@ -50,7 +50,7 @@ def test_noalloc_matches_allocating_entry_on_two_calls():
         args = (meta.kv_indices.shape[1], 64, _lib.ptr(meta.kv_indices), _lib.ptr(meta.kv_flags), _lib.ptr(meta.kv_counts))
         rc = lib.hb_paired_fwd(
             _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(ref), _strides(q, k, v, ref), 1, 4, N, 128, G, *args,
-            scale_log2, 1, _lib.ptr(workspace), ws_bytes, ctypes.c_void_p(stream),
+            scale_log2, 1, None, _lib.ptr(workspace), ws_bytes, ctypes.c_void_p(stream),
         )
         assert rc == 0, _lib.status_text(rc)
         rc = lib.hb_paired_fwd_noalloc(
