@@ -246,6 +246,8 @@ def run_native(a):
     weighted_flop = sum(w * f for w, f in zip(WEIGHTS, flops)) / 57
     value = sum(flops) * a.steps / (total_ms * 1e-3) / 1e12
 
+    perm = permutation_side_timing(a, q, k, v, metas, plan, dev, hb) if world == 1 else None
+
     e2e = None
     if not a.no_e2e:
         e2e = run_e2e(a, q, k, v, metas, flops, world, dev, hb)
@@ -300,6 +302,8 @@ def run_native(a):
             "kernel": "k_paired_fwd",
         },
     }
+    if perm is not None:
+        line["token_order"] = perm
     if e2e is not None:
         line["e2e"] = e2e
     if clk.result is not None:
@@ -307,6 +311,44 @@ def run_native(a):
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def permutation_side_timing(a, q, k, v, metas, plan, dev, hb, steps=5):
+    """Raster-order Q/K/V (the tensors as given, read as raster token order):
+    mean ms per call of the fused gather/scatter (``token_order``) against the
+    explicit path (index_select of Q/K/V into the plan's order, the kernel,
+    scatter of O back; sampling_layout.py:88-116 per call)."""
+    from hilberta_b200.paired_kernel import token_order_map
+
+    rows = token_order_map(plan, dev)
+    idx = rows.long()
+    out = torch.empty_like(q)
+    kw = dict(global_strategy="triton", num_warps=8, num_stages=2)
+
+    def fused(ph):
+        hb.paired_attention(q, k, v, metas[ph], out=out, token_order=rows, **kw)
+
+    def explicit(ph):
+        pq, pk, pv = (x.index_select(2, idx) for x in (q, k, v))
+        o = hb.paired_attention(pq, pk, pv, metas[ph], **kw)
+        out[:, :, idx] = o
+
+    res = {}
+    with torch.inference_mode():
+        for name, fn in (("fused_ms_per_call", fused), ("explicit_ms_per_call", explicit)):
+            for ph in range(4):
+                fn(ph)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                for ph in range(4):
+                    fn(ph)
+            e1.record()
+            torch.cuda.synchronize()
+            res[name] = round(e0.elapsed_time(e1) / (4 * steps), 4)
+    res["note"] = "Q/K/V in raster token order; fused = gather/scatter inside k_paired_fwd (tile::gather4)"
+    return res
 
 
 def run_e2e(a, q, k, v, metas, flops, world, dev, hb):
