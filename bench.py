@@ -10,9 +10,12 @@ the plan); ms/call is phase-weighted 15/14/14/14 over 57 layers
 (benchmark.py:76-83).  FLOP per call = H * 4*64*64*D * A, A = active 64x64
 (query-block, key-block) pairs (global rows x all blocks + sum of kv_counts).
 
-N > 1 (torchrun): head-parallel, rank r owns heads [r*H/P, (r+1)*H/P); a step
-adds the NCCL all-gather of the bf16 head outputs (what the FLUX block consumes);
-``value`` = total active FLOP of all ranks / max-over-ranks device time.
+N > 1 (torchrun): head-parallel, rank r owns heads [r*H/P, (r+1)*H/P); every
+call also gathers all ranks' bf16 head outputs on every rank (what the FLUX
+block consumes) — inside the attention kernel, which stores each output row to
+all ranks over NVLink peer memory (head_parallel.PeerAllGather).  ``value`` =
+total active FLOP of all ranks / max-over-ranks device time.  The kernel
+followed by an NCCL all-gather is timed beside it (``nccl_path``).
 
 ``--impl reference`` times the reference's dense-mask CPU path (plan mask +
 fp32 SDPA, the computation of hilberta/flux_adapter.py:299-307) restated in
@@ -199,21 +202,24 @@ def run_native(a):
     N = plan.total_tokens
     q, k, v = (x.to(dev) for x in qkv_host)
     out = torch.empty_like(q)
-    gathered = torch.empty(world, 1, hr, N, 128, dtype=torch.bfloat16, device=dev) if world > 1 else None
     stream = torch.cuda.current_stream(dev)
+    kw = dict(global_strategy="triton", num_warps=8, num_stages=2)
+    fused = None
+    if world > 1:
+        from hilberta_b200.head_parallel import PeerAllGather
+
+        fused = PeerAllGather(1, H, N, 128, layout=a.layout, device=dev)
 
     def call(ph):
-        hb.paired_attention(q, k, v, metas[ph], global_strategy="triton", num_warps=8, num_stages=2, out=out)
-
-    def gather():
-        if world > 1:
-            dist.all_gather_into_tensor(gathered.view(-1), out.contiguous().view(-1))
+        if fused is None:
+            hb.paired_attention(q, k, v, metas[ph], out=out, **kw)
+        else:
+            fused(q, k, v, metas[ph], **kw)
 
     with torch.inference_mode():
         for _ in range(max(3, a.warmup)):
             for ph in range(4):
                 call(ph)
-                gather()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -228,7 +234,6 @@ def run_native(a):
                     ev[s][ph][0].record(stream)
                     call(ph)
                     ev[s][ph][1].record(stream)
-                    gather()
             t1.record(stream)
             torch.cuda.synchronize()
             if world > 1:
@@ -247,18 +252,19 @@ def run_native(a):
     value = sum(flops) * a.steps / (total_ms * 1e-3) / 1e12
 
     perm = permutation_side_timing(a, q, k, v, metas, plan, dev, hb) if world == 1 else None
+    nccl = nccl_side_timing(a, q, k, v, metas, flops, world, dev, hb) if world > 1 else None
 
     e2e = None
     if not a.no_e2e:
-        e2e = run_e2e(a, q, k, v, metas, flops, world, dev, hb)
+        e2e = run_e2e(a, q, k, v, metas, flops, world, dev, hb, fused)
     peak, hbm, peak_kind = peaks()
     achieved = weighted_flop / world / (weighted_ms * 1e-3) / 1e12  # one GPU's launch
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(a, plan, active, bounded=a.cpu_seconds)
     if world > 1:
+        fused.close()
         dist.barrier()
-        del gathered
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -284,7 +290,8 @@ def run_native(a):
             "workload": f"HilbertA paired sparse attention {a.config}, B=1, H={H}, D=128, N={N}, G=512",
             "layout": a.layout,
             "heads_per_gpu": hr,
-            "step": "4 calls (tile phases 0-3)" + (" each + NCCL all-gather of head outputs" if world > 1 else ""),
+            "step": "4 calls (tile phases 0-3)"
+            + (", each fused with the all-gather of head outputs over NVLink peer memory" if world > 1 else ""),
             "parallelism": f"head-parallel x{world}" if world > 1 else "single GPU",
             "l2": "inputs larger than L2 (Q+K+V %.0f MB)" % (3 * N * H * 128 * 2 / 1e6),
             "active_blocks_per_phase": active,
@@ -304,6 +311,21 @@ def run_native(a):
     }
     if perm is not None:
         line["token_order"] = perm
+    if world > 1:
+        # fused compute + collective: the target is the slower of the tensor time
+        # and this GPU's share of the NVLink traffic (its rows to P-1 peers)
+        link = 770.0  # GB/s per direction, measured peer copy on this pool
+        nv_bytes = (world - 1) * N * hr * 128 * 2
+        t_tensor = weighted_flop / world / (peak * 1e12)
+        t_link = nv_bytes / (link * 1e9)
+        line["roofline"]["fused_allgather"] = {
+            "nvlink_bytes_per_call": nv_bytes,
+            "link_gbs": link,
+            "target_ms": round(max(t_tensor, t_link) * 1e3, 4),
+            "bound": "tensor" if t_tensor >= t_link else "nvlink",
+            "frac": round(max(t_tensor, t_link) * 1e3 / weighted_ms, 4),
+        }
+        line["nccl_path"] = nccl
     if e2e is not None:
         line["e2e"] = e2e
     if clk.result is not None:
@@ -311,6 +333,50 @@ def run_native(a):
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def nccl_side_timing(a, q, k, v, metas, flops, world, dev, hb, steps=5):
+    """The unfused head-parallel path on the same inputs: the kernel into a local
+    output, then an NCCL all-gather of every rank's heads (max over ranks)."""
+    import torch.distributed as dist
+
+    out = torch.empty_like(q)
+    B, hr, N, D = q.shape
+    gathered = torch.empty(world, B, hr, N, D, dtype=q.dtype, device=dev)
+    kw = dict(global_strategy="triton", num_warps=8, num_stages=2)
+    ev = []
+    with torch.inference_mode():
+        def step(record):
+            for ph in range(4):
+                e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) if record else None
+                if e:
+                    e[0].record()
+                hb.paired_attention(q, k, v, metas[ph], out=out, **kw)
+                if e:
+                    e[1].record()
+                    ev.append(e)
+                dist.all_gather_into_tensor(gathered.view(-1), out.contiguous().view(-1))
+
+        for _ in range(3):
+            step(False)
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            step(True)
+        t1.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([t0.elapsed_time(t1) / steps, statistics.mean(e[0].elapsed_time(e[1]) for e in ev)],
+                     dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    return {
+        "ms_per_step": round(float(t[0]), 4),
+        "kernel_ms_per_call": round(float(t[1]), 4),
+        "value": round(sum(flops) / (float(t[0]) * 1e-3) / 1e12, 2),
+        "note": "paired_attention into a local output, then dist.all_gather_into_tensor (NCCL), per call",
+    }
 
 
 def permutation_side_timing(a, q, k, v, metas, plan, dev, hb, steps=5):
@@ -351,23 +417,30 @@ def permutation_side_timing(a, q, k, v, metas, plan, dev, hb, steps=5):
     return res
 
 
-def run_e2e(a, q, k, v, metas, flops, world, dev, hb):
+def run_e2e(a, q, k, v, metas, flops, world, dev, hb, fused=None):
     """Same metric through the public call with HOST buffers: per call, pinned
-    Q/K/V host->device, paired_attention, output device->host."""
+    Q/K/V host->device, the attention (at N > 1 this rank's heads fused with the
+    all-gather, PeerAllGather), and the output this rank consumes (all heads at
+    N > 1) device->host."""
     import torch.distributed as dist
 
     hq, hk, hv = (x.detach().cpu().contiguous().pin_memory() for x in (q, k, v))
-    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    B, hr, N, D = q.shape
+    hout = torch.empty((B, hr * world, N, D), dtype=q.dtype).pin_memory()
     dq, dk, dv = (torch.empty_like(x, device=dev) for x in (hq, hk, hv))
     dout = torch.empty_like(dq)
     steps = max(1, min(a.steps, 5))
+    kw = dict(global_strategy="triton", num_warps=8, num_stages=2)
 
     def one(ph):
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
-        hb.paired_attention(dq, dk, dv, metas[ph], global_strategy="triton", num_warps=8, num_stages=2, out=dout)
-        hout.copy_(dout, non_blocking=True)
+        if fused is None:
+            res = hb.paired_attention(dq, dk, dv, metas[ph], out=dout, **kw)
+        else:
+            res = fused(dq, dk, dv, metas[ph], **kw)
+        hout.copy_(res, non_blocking=True)
 
     with torch.inference_mode():
         for ph in range(4):
@@ -395,7 +468,8 @@ def run_e2e(a, q, k, v, metas, flops, world, dev, hb):
         "h2d_bytes_per_step": h2d,
         "d2h_bytes_per_step": d2h,
         "steps": steps,
-        "note": "per call: pinned Q/K/V H2D + paired_attention + O D2H, through hilberta_b200.paired_attention",
+        "note": "per call: pinned Q/K/V H2D + attention + O D2H through the public API"
+        + (" (head_parallel.PeerAllGather: local heads in, all heads out)" if fused is not None else " (paired_attention)"),
     }
 
 

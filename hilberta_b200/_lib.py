@@ -30,6 +30,10 @@ HB_ERR_TMA = -9
 HB_DEV_TIMEOUT = 1
 HB_DEV_BAD_COUNT = 2
 HB_DEV_BAD_BLOCK = 4
+HB_DEV_PEER_TIMEOUT = 8
+
+HB_MAX_RANKS = 8
+HB_IPC_HANDLE_BYTES = 64
 
 # Every exported symbol of include/hilberta_b200.h (checked by the CPU tests).
 EXPORTS = (
@@ -45,6 +49,10 @@ EXPORTS = (
     "hb_fwd_workspace_bytes_for",
     "hb_paired_fwd",
     "hb_paired_fwd_noalloc",
+    "hb_paired_fwd_allgather",
+    "hb_ipc_export",
+    "hb_ipc_open",
+    "hb_ipc_close",
 )
 
 
@@ -58,6 +66,19 @@ class PlanDims(ctypes.Structure):
         ("rows", ctypes.c_int64),
         ("row_capacity", ctypes.c_int64),
         ("workspace_bytes", ctypes.c_int64),
+    ]
+
+
+class PeerOut(ctypes.Structure):
+    """hb_peer_out_t: every rank's output view and flag words for the fused all-gather."""
+
+    _fields_ = [
+        ("n_ranks", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("epoch", ctypes.c_int32),
+        ("timeout_ms", ctypes.c_int32),
+        ("out", ctypes.c_void_p * HB_MAX_RANKS),
+        ("flags", ctypes.c_void_p * HB_MAX_RANKS),
     ]
 
 
@@ -80,6 +101,14 @@ _SIGS = {
         [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P,
          _P, ctypes.c_size_t, _P],
     ),
+    "hb_paired_fwd_allgather": (
+        _I,
+        [_P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I,
+         ctypes.POINTER(PeerOut), _P, ctypes.c_size_t, _P],
+    ),
+    "hb_ipc_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
+    "hb_ipc_open": (_I, [_P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
+    "hb_ipc_close": (_I, [_P, ctypes.c_uint64]),
     "hb_paired_fwd_noalloc": (
         _I,
         [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P],

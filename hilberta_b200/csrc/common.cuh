@@ -5,10 +5,15 @@
 
 #include "../../include/hilberta_b200.h"
 
+// On failure the runtime's last-error slot is cleared too, so a later launch
+// check does not report this call's (non-sticky) error as its own.
 #define HB_CUDA_TRY(expr)                                  \
     do {                                                   \
         cudaError_t _e = (expr);                           \
-        if (_e != cudaSuccess) return HB_ERR_CUDA;         \
+        if (_e != cudaSuccess) {                           \
+            (void)cudaGetLastError();                      \
+            return HB_ERR_CUDA;                            \
+        }                                                  \
     } while (0)
 
 #define HB_LAUNCH_CHECK() HB_CUDA_TRY(cudaGetLastError())

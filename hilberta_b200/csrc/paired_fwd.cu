@@ -46,7 +46,6 @@ struct FwdParams {
     CUtensorMap tmap_k;
     CUtensorMap tmap_v;
     int32_t perm_q[3], perm_k[3], perm_v[3];  // tensor-map dim (1..3) holding (n, h, b)
-    void* out;
     int64_t o_sb, o_sh, o_sn;
     const int32_t* indices;
     const int32_t* flags;
@@ -69,6 +68,14 @@ struct FwdParams {
     // gathered tensor maps are 2-D (D, rows); rs_* = (b, h, n) strides in rows.
     const int32_t* row_map;
     int64_t rs_q[3], rs_k[3], rs_v[3];
+    // Output rows go to n_out tensors (same strides o_s*): `out` alone, or every
+    // rank's full-head output at this rank's first head (fused all-gather).  In
+    // the latter mode (n_out > 1) the last CTA signals flags[i][rank] = epoch on
+    // every rank i and waits for flags[rank][i] from all of them.
+    int n_out, rank, epoch;
+    void* outs[HB_MAX_RANKS];
+    int32_t* peer_flags[HB_MAX_RANKS];
+    long long peer_timeout;  // SM cycles the completion wait may take
     float scale_log2;
     long long timeout;  // SM cycles a single barrier wait may take
 };
@@ -504,24 +511,61 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
         if (!warp_wait(bar_o_done, gl & 1, abort_flag, p.timeout)) return;
         tc_fence_after();
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh +
-                  (int64_t)(p.row_map ? p.row_map[w.qrow0 + r] : w.qrow0 + r) * p.o_sn;
-        const bool vec = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
+        const int64_t ooff = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh +
+                             (int64_t)(p.row_map ? p.row_map[w.qrow0 + r] : w.qrow0 + r) * p.o_sn;
+        // every destination has the same address residue mod 16 (checked on the host)
+        const bool vec = (reinterpret_cast<uintptr_t>(reinterpret_cast<T*>(p.outs[0]) + ooff) & 15) == 0;
+        // Rows are written to this rank's output first (lane = row); with vector
+        // alignment, push_rows then copies the warp's finished rows to the other
+        // ranks with lane-consecutive 16-byte stores (whole rows per instruction,
+        // the shape that keeps NVLink writes full), re-reading them from L2.
+        const bool push = p.n_out > 1 && vec;
         auto store_row = [&](int c, const float* vals) {  // 32 output columns from 32 fp32 values
             uint32_t packed[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) packed[i] = pack2<BF16>(vals[2 * i], vals[2 * i + 1]);
-            if (vec) {
-                uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+            for (int d = 0; d < p.n_out; d++) {
+                if (d != p.rank && push) continue;
+                T* orow = reinterpret_cast<T*>(p.outs[d]) + ooff;
+                if (vec) {
+                    uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
 #pragma unroll
-                for (int i = 0; i < 4; i++)
-                    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-            } else {
-                uint16_t* dst = reinterpret_cast<uint16_t*>(orow + 32 * c);
+                    for (int i = 0; i < 4; i++)
+                        dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                } else {
+                    uint16_t* dst = reinterpret_cast<uint16_t*>(orow + 32 * c);
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    dst[2 * i] = (uint16_t)(packed[i] & 0xffffu);
-                    dst[2 * i + 1] = (uint16_t)(packed[i] >> 16);
+                    for (int i = 0; i < 16; i++) {
+                        dst[2 * i] = (uint16_t)(packed[i] & 0xffffu);
+                        dst[2 * i + 1] = (uint16_t)(packed[i] >> 16);
+                    }
+                }
+            }
+        };
+        auto push_rows = [&]() {  // the warp's 32 rows, already in outs[rank], to every other rank
+            constexpr int CPR = D / 8;     // 16-byte chunks per row
+            constexpr int RPI = 32 / CPR;  // rows per warp instruction
+            __syncwarp();                  // the lanes' row stores are visible to the whole warp
+            const int row0 = w.qrow0 + (r & ~31) + lane / CPR;
+            const int64_t hb_off = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh;
+            const T* src = reinterpret_cast<const T*>(p.outs[p.rank]);
+            // loads in batches of 8 ahead of their stores: the destinations could
+            // alias the source as far as the compiler knows, so interleaving
+            // would serialise every load behind the previous store
+            constexpr int NI = 32 / RPI, BATCH = NI < 8 ? NI : 8;
+#pragma unroll
+            for (int i0 = 0; i0 < NI; i0 += BATCH) {
+                uint4 v4[BATCH];
+#pragma unroll
+                for (int i = 0; i < BATCH; i++)
+                    v4[i] = __ldcg(reinterpret_cast<const uint4*>(src + hb_off + (int64_t)(row0 + (i0 + i) * RPI) * p.o_sn) +
+                                   lane % CPR);
+                for (int d = 0; d < p.n_out; d++) {
+                    if (d == p.rank) continue;
+                    T* dst = reinterpret_cast<T*>(p.outs[d]) + hb_off;
+#pragma unroll
+                    for (int i = 0; i < BATCH; i++)
+                        *(reinterpret_cast<uint4*>(dst + (int64_t)(row0 + (i0 + i) * RPI) * p.o_sn) + lane % CPR) = v4[i];
                 }
             }
         };
@@ -539,6 +583,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_o_empty);
+            if (push) push_rows();
         } else {
             constexpr int PSTRIDE = 128 * D + 256;
             float* rec = p.partial + ((int64_t)w.group * p.n_chunks + w.chunk) * PSTRIDE;
@@ -605,9 +650,29 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                     for (int i = 0; i < 32; i++) vals[i] *= inv;
                     store_row(c, vals);
                 }
+                if (push) push_rows();
             }
         }
         g += w.n;
+    }
+}
+
+// Fused all-gather completion, run by one thread after every CTA of the launch
+// has stored its rows and fenced them at system scope: publish this rank's
+// epoch to every rank, then wait (bounded) for every rank's epoch here.
+__device__ __noinline__ void peer_complete(const FwdParams& p) {
+    __threadfence_system();
+    for (int i = 0; i < p.n_out; i++) st_release_sys(p.peer_flags[i] + p.rank, p.epoch);
+    const int32_t* mine = p.peer_flags[p.rank];
+    const long long t0 = clock64();
+    for (int i = 0; i < p.n_out; i++) {
+        // epochs only grow: compare by wrap-safe difference
+        while ((int32_t)((uint32_t)ld_acquire_sys(mine + i) - (uint32_t)p.epoch) < 0) {
+            if (clock64() - t0 > p.peer_timeout) {
+                atomicOr(&p.ws[2], HB_DEV_PEER_TIMEOUT);
+                return;
+            }
+        }
     }
 }
 
@@ -692,12 +757,20 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
     }
     if (threadIdx.x == 0) {
         if (abort_sh) atomicOr(&p.ws[2], HB_DEV_TIMEOUT);
-        __threadfence();
+        // The CTA's row stores (all threads, ordered before this thread by the
+        // barrier above) are made visible at the scope the consumers need before
+        // the CTA is counted: one fence per CTA (a system-scope fence in every
+        // thread costs milliseconds per launch).
+        if (p.n_out > 1)
+            __threadfence_system();
+        else
+            __threadfence();
         const int prev = atomicAdd(&p.ws[1], 1);
         if (prev == (int)gridDim.x - 1) {  // last CTA: reset the work counter for the next launch
             atomicExch(&p.ws[0], 0);
             atomicExch(&p.ws[1], 0);
             __threadfence();
+            if (p.n_out > 1) peer_complete(p);
         }
     }
 }
@@ -794,26 +867,40 @@ int make_tmap_rows(CUtensorMap* map, const void* base, bool bf16, int D, int N, 
 
 struct DeviceInfo {
     int sms = 0;
+    int clock_khz = 0;
     bool configured[8] = {false, false, false, false, false, false, false, false};
 };
 std::mutex g_mu;
 DeviceInfo g_dev[64];
+
+// SM count and SM clock of a device, queried once (the attribute queries are
+// not free, and the launch path runs once per attention call).
+int device_info(int dev, int* sms, int* clock_khz) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceInfo& di = g_dev[dev];
+    if (!di.sms) {
+        HB_CUDA_TRY(cudaDeviceGetAttribute(&di.clock_khz, cudaDevAttrClockRate, dev));
+        HB_CUDA_TRY(cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev));
+    }
+    if (sms) *sms = di.sms;
+    if (clock_khz) *clock_khz = di.clock_khz;
+    return HB_OK;
+}
 
 template <int D, bool BF16, bool GATHER>
 int launch(const FwdParams& p, int dev, cudaStream_t st) {
     using C = Cfg<D>;
     auto kern = k_paired_fwd<D, BF16, GATHER>;
     const int slot = (D == 128 ? 2 : 0) + (BF16 ? 1 : 0) + (GATHER ? 4 : 0);
-    int sms;
+    int sms, rc;
+    if ((rc = device_info(dev, &sms, nullptr))) return rc;
     {
         std::lock_guard<std::mutex> lk(g_mu);
         DeviceInfo& di = g_dev[dev];
-        if (!di.sms) HB_CUDA_TRY(cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev));
         if (!di.configured[slot]) {
             HB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
             di.configured[slot] = true;
         }
-        sms = di.sms;
     }
     const int grid = std::min(p.num_items, 2 * sms);
     kern<<<grid, 256, C::SMEM, st>>>(p);
@@ -869,11 +956,27 @@ extern "C" size_t hb_fwd_workspace_bytes_for(int B, int H, int N, int G, int D) 
     return (size_t)std::max<int64_t>(WS_HEADER, split_plan(B, H, N, G, D).bytes);
 }
 
-extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides, int B,
-                             int H, int N, int D, int G, int W, int key_block_size, const int32_t* kv_indices,
-                             const int32_t* kv_flags, const int32_t* kv_counts, float scale_log2, int dtype,
-                             const int32_t* row_map, void* workspace, size_t workspace_bytes, void* stream_) {
-    if (!q || !k || !v || !out || !strides || !workspace) return HB_ERR_ARG;
+namespace hb {
+namespace {
+// Shared body of hb_paired_fwd (out, optional row_map) and hb_paired_fwd_allgather
+// (peers: every rank's output and flag words).
+int paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides, int B, int H, int N,
+               int D, int G, int W, int key_block_size, const int32_t* kv_indices, const int32_t* kv_flags,
+               const int32_t* kv_counts, float scale_log2, int dtype, const int32_t* row_map,
+               const hb_peer_out_t* peers, void* workspace, size_t workspace_bytes, void* stream_) {
+    if (!q || !k || !v || !(out || peers) || !strides || !workspace) return HB_ERR_ARG;
+    if (peers) {
+        const int n = peers->n_ranks;
+        if (n < 1 || n > HB_MAX_RANKS || peers->rank < 0 || peers->rank >= n || peers->epoch <= 0 ||
+            peers->timeout_ms < 0)
+            return HB_ERR_ARG;
+        for (int i = 0; i < n; i++) {
+            if (!peers->out[i] || !peers->flags[i] || (reinterpret_cast<uintptr_t>(peers->flags[i]) & 3))
+                return HB_ERR_ARG;
+            if (((reinterpret_cast<uintptr_t>(peers->out[i]) ^ reinterpret_cast<uintptr_t>(peers->out[0])) & 15))
+                return HB_ERR_ARG;  // one vector-store decision serves every destination
+        }
+    }
     if (row_map && (reinterpret_cast<uintptr_t>(row_map) & 15)) return HB_ERR_ARG;
     if (workspace_bytes < hb_fwd_workspace_bytes() || (reinterpret_cast<uintptr_t>(workspace) & 255))
         return HB_ERR_WORKSPACE;
@@ -904,7 +1007,23 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
         if ((rc = make_tmap(&p.tmap_k, k, bf16, D, N, H, B, strides[3], strides[4], strides[5], 64, p.perm_k))) return rc;
         if ((rc = make_tmap(&p.tmap_v, v, bf16, D, N, H, B, strides[6], strides[7], strides[8], 64, p.perm_v))) return rc;
     }
-    p.out = out;
+    if (peers) {
+        const int n = peers->n_ranks;
+        for (int i = 0; i < n; i++) {
+            p.outs[i] = peers->out[i];
+            p.peer_flags[i] = peers->flags[i];
+        }
+        p.n_out = n;
+        p.rank = peers->rank;
+        p.epoch = peers->epoch;
+        int khz = 0;
+        if ((rc = device_info(dev, nullptr, &khz))) return rc;
+        const long long ms = peers->timeout_ms ? peers->timeout_ms : 10000;
+        p.peer_timeout = ms * (long long)(khz > 0 ? khz : 2000000);
+    } else {
+        p.outs[0] = out;
+        p.n_out = 1;
+    }
     p.o_sb = strides[9];
     p.o_sh = strides[10];
     p.o_sn = strides[11];
@@ -927,7 +1046,7 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
     int n_chunks = 1;
     if (sp.n_chunks > 1 && split_fits(sp, (int64_t)workspace_bytes)) {
         int sms = 0;
-        HB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        if ((rc = device_info(dev, &sms, nullptr))) return rc;
         const double share = (double)B * H * ((double)p.g_rows * p.nkb + (double)o_rows * W) / (2.0 * sms);
         const int target = std::max(CHUNK_BLOCKS, (int)(0.75 * share));
         n_chunks = std::min(sp.n_chunks, (p.nkb + target - 1) / target);
@@ -951,6 +1070,27 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
     }
     if (D == 128) return bf16 ? launch<128, true, false>(p, dev, st) : launch<128, false, false>(p, dev, st);
     return bf16 ? launch<64, true, false>(p, dev, st) : launch<64, false, false>(p, dev, st);
+}
+}  // namespace
+}  // namespace hb
+
+extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides, int B,
+                             int H, int N, int D, int G, int W, int key_block_size, const int32_t* kv_indices,
+                             const int32_t* kv_flags, const int32_t* kv_counts, float scale_log2, int dtype,
+                             const int32_t* row_map, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!out) return HB_ERR_ARG;
+    return paired_fwd(q, k, v, out, strides, B, H, N, D, G, W, key_block_size, kv_indices, kv_flags, kv_counts,
+                      scale_log2, dtype, row_map, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int hb_paired_fwd_allgather(const void* q, const void* k, const void* v, const int64_t* strides, int B,
+                                       int H, int N, int D, int G, int W, int key_block_size,
+                                       const int32_t* kv_indices, const int32_t* kv_flags, const int32_t* kv_counts,
+                                       float scale_log2, int dtype, const hb_peer_out_t* peers, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+    if (!peers) return HB_ERR_ARG;
+    return paired_fwd(q, k, v, nullptr, strides, B, H, N, D, G, W, key_block_size, kv_indices, kv_flags, kv_counts,
+                      scale_log2, dtype, nullptr, peers, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------

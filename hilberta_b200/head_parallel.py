@@ -6,16 +6,24 @@ attention shards by heads with no collective inside it: rank r of P owns heads
 [r*H/P, (r+1)*H/P) (24 heads -> 12/6/3 per GPU at P = 2/4/8), with the metadata
 replicated.  The one exchange is an all-gather of the 16-bit head outputs where
 the FLUX block needs every head (before ``to_out``,
-hilberta/flux_adapter.py:328-339), issued through torch.distributed (NCCL over
-NVLink on GPUs; gloo works for host-side tests).
+hilberta/flux_adapter.py:328-339):
+
+* ``PeerAllGather`` (the B200 path): the attention kernel itself stores every
+  output row into all ranks' full-head outputs over NVLink peer memory, so the
+  exchange overlaps the math; a bounded device-side flag barrier ends the call.
+* ``all_gather_heads`` / ``head_parallel_attention``: the kernel followed by a
+  torch.distributed all-gather (NCCL on GPUs; gloo for host-side tests).
 """
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from .paired_kernel import paired_attention
+from . import _lib
+from .paired_kernel import LOG2E, _check_inputs, _launch_allgather, paired_attention  # noqa: F401
 
 
 def head_range(num_heads: int, rank: int, world: int) -> tuple[int, int]:
@@ -72,3 +80,106 @@ def head_parallel_attention(q, k, v, metadata, *, group=None, gather=True, layou
     if not gather:
         return out
     return all_gather_heads(out, group=group, layout=layout)
+
+
+class PeerAllGather:
+    """Paired attention of this rank's heads fused with the all-gather of all
+    ranks' heads (``hb_paired_fwd_allgather``).
+
+    Collective: every rank of `group` (one process per GPU, distinct GPUs of one
+    node) constructs it with the same arguments and then makes the same sequence
+    of calls.  ``heads`` is the total head count; each call takes this rank's
+    head slice ``[B, heads/P, N, D]`` and returns the full ``[B, heads, N, D]``
+    output (a view of storage in ``layout`` order: "bhnd", or "bnhd" as the
+    processor's hidden states before ``flatten(2, 3)``), complete on return of
+    the launch on the current stream.  Outputs alternate between two buffers, so
+    a returned tensor stays valid until the call after next.  After a call that
+    reports ``HB_DEV_PEER_TIMEOUT`` (``device_status``) the ranks' flags may
+    disagree: close the instance and build a new one.
+    """
+
+    def __init__(self, batch, heads, tokens, head_dim, *, dtype=torch.bfloat16, layout="bhnd", group=None,
+                 device=None, timeout_ms=10000):
+        world, rank = _world(group)
+        if world > _lib.HB_MAX_RANKS:
+            raise ValueError(f"at most {_lib.HB_MAX_RANKS} ranks")
+        if layout not in ("bhnd", "bnhd"):
+            raise ValueError("layout must be bhnd or bnhd")
+        self.head0, self.head1 = head_range(heads, rank, world)
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.world, self.rank, self.group, self.device = world, rank, group, dev
+        self.shape = (batch, heads, tokens, head_dim)
+        self.dtype, self.timeout_ms = dtype, int(timeout_ms)
+        ids = [None] * world
+        dist.all_gather_object(ids, str(torch.cuda.get_device_properties(dev).uuid), group=group)
+        if len(set(ids)) != world:
+            raise ValueError("PeerAllGather needs every rank on a distinct GPU")
+        store = (batch, heads, tokens, head_dim) if layout == "bhnd" else (batch, tokens, heads, head_dim)
+        with torch.inference_mode(False):
+            self._bufs = [torch.empty(store, dtype=dtype, device=dev) for _ in range(2)]
+            self._flags = torch.zeros(_lib.HB_MAX_RANKS, dtype=torch.int32, device=dev)
+        self._views = [b if layout == "bhnd" else b.transpose(1, 2) for b in self._bufs]
+        torch.cuda.synchronize(dev)  # flags are zero before any peer can write them
+        lib = _lib.lib()
+        mine = []
+        for t in (*self._bufs, self._flags):
+            h = ctypes.create_string_buffer(_lib.HB_IPC_HANDLE_BYTES)
+            off = ctypes.c_uint64()
+            _lib.check(lib.hb_ipc_export(ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off)), "hb_ipc_export")
+            mine.append((h.raw, off.value))
+        everyone = [None] * world
+        dist.all_gather_object(everyone, mine, group=group)
+        self._opened = {}  # handle bytes -> mapped allocation base (one mapping per peer allocation)
+        self._ptrs = []  # rank -> [buf0, buf1, flags] device addresses usable on this GPU
+        for r, handles in enumerate(everyone):
+            if r == rank:
+                self._ptrs.append([t.data_ptr() for t in (*self._bufs, self._flags)])
+                continue
+            ptrs = []
+            for h, off in handles:
+                if h not in self._opened:
+                    base = ctypes.c_void_p()
+                    _lib.check(lib.hb_ipc_open(h, 0, ctypes.byref(base)), "hb_ipc_open")
+                    self._opened[h] = base.value
+                ptrs.append(self._opened[h] + off)
+            self._ptrs.append(ptrs)
+        dist.barrier(group=group)  # every rank mapped every peer before the first call
+        self.epoch = 0
+
+    def __call__(self, q, k, v, metadata, *, global_strategy="flash", num_warps=4, num_stages=2, scale=None):
+        if self._ptrs is None:
+            raise RuntimeError("PeerAllGather is closed")
+        B, H, N, D = self.shape
+        N_, G, scale = _check_inputs(q, k, v, metadata, global_strategy, num_warps, num_stages, scale)
+        if q.shape != (B, self.head1 - self.head0, N, D) or q.dtype != self.dtype or q.device != self.device:
+            raise ValueError("Q/K/V must be this rank's [B, heads/P, N, D] slice in the gather's dtype and device")
+        self.epoch += 1
+        slot = self.epoch & 1
+        full = self._views[slot]
+        elem = full.element_size()
+        peers = _lib.PeerOut()
+        peers.n_ranks, peers.rank, peers.epoch, peers.timeout_ms = self.world, self.rank, self.epoch, self.timeout_ms
+        for r in range(self.world):
+            peers.out[r] = self._ptrs[r][slot] + self.head0 * full.stride(1) * elem
+            peers.flags[r] = self._ptrs[r][2]
+        _launch_allgather(q, k, v, full, metadata, N_, G, scale, peers)
+        return full
+
+    def close(self):
+        """Unmap the peers' buffers once every rank is done with every call (collective)."""
+        if self._ptrs is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        lib = _lib.lib()
+        for base in self._opened.values():
+            _lib.check(lib.hb_ipc_close(ctypes.c_void_p(base), 0), "hb_ipc_close")
+        self._opened, self._ptrs = {}, None
+        dist.barrier(group=self.group)  # no rank frees its buffers while a peer still maps them
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+        return False

@@ -77,6 +77,27 @@ def _launch(q, k, v, out, metadata, N, G, scale, row_map=None):
     _lib.check(rc, "hb_paired_fwd")
 
 
+def _launch_allgather(q, k, v, full, metadata, N, G, scale, peers):
+    """hb_paired_fwd_allgather: `full` is this rank's [B, H_all, N, D] view (its
+    strides describe every rank's output); `peers` an _lib.PeerOut."""
+    dev = q.device
+    stream = torch.cuda.current_stream(dev)
+    B, H, _, D = q.shape
+    lib = _lib.lib()
+    ws = _workspace(dev, stream.cuda_stream, lib.hb_fwd_workspace_bytes_for(B, H, N, G, D))
+    strides = (ctypes.c_int64 * 12)(*q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *full.stride()[:3])
+    rc = lib.hb_paired_fwd_allgather(
+        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), strides, B, H, N, D, G,
+        int(metadata.kv_indices.shape[1]), int(metadata.key_block_size),
+        _lib.ptr(metadata.kv_indices), _lib.ptr(metadata.kv_flags), _lib.ptr(metadata.kv_counts),
+        float(scale * LOG2E), 1 if q.dtype == torch.bfloat16 else 0, ctypes.byref(peers), _lib.ptr(ws),
+        ws.numel() * 4, ctypes.c_void_p(stream.cuda_stream),
+    )
+    if rc == _lib.HB_ERR_TMA:
+        raise ValueError("Q/K/V need 16-byte aligned base pointers and strides for TMA tiles")
+    _lib.check(rc, "hb_paired_fwd_allgather")
+
+
 def token_order_map(plan, device) -> torch.Tensor:
     """Physical -> raster row map of a plan for ``paired_attention(token_order=...)``:
     text rows first (identity), then ``text_tokens + image_order`` (plan.py:147)."""
@@ -101,6 +122,39 @@ def paired_attention(
     kernel then gathers rows while loading and scatters output rows, replacing
     the reference's separate reorder pass (sampling_layout.py:88-116).
     """
+    N, G, scale = _check_inputs(q, k, v, metadata, global_strategy, num_warps, num_stages, scale)
+    if out is not None:
+        if out.shape != q.shape or out.dtype != q.dtype or out.device != q.device or out.stride(-1) != 1:
+            raise ValueError("Output must match Q shape/dtype/device with contiguous D")
+        if any(s <= 0 for s in out.stride()) or not _non_overlapping_strides(out):
+            raise ValueError("Positive non-overlapping output strides required")
+        if torch.is_grad_enabled() and out.requires_grad:
+            raise ValueError("Inference output cannot require gradients")
+        begin, end = _tensor_byte_span(out)
+        for x in (q, k, v, metadata.kv_indices, metadata.kv_flags, metadata.kv_counts):
+            first, last = _tensor_byte_span(x)
+            if begin < last and first < end:
+                raise ValueError("Output cannot alias inputs or metadata")
+    else:
+        out = torch.empty_like(q)
+    if token_order is not None:
+        if (
+            not isinstance(token_order, torch.Tensor)
+            or token_order.dtype != torch.int32
+            or token_order.device != q.device
+            or token_order.shape != (N,)
+            or not token_order.is_contiguous()
+        ):
+            raise ValueError("token_order must be a contiguous int32 [N] tensor on the Q device")
+        if any(s % q.shape[-1] for x in (q, k, v) for s in x.stride()[:3]):
+            raise ValueError("token_order needs Q/K/V outer strides that are multiples of D")
+    _launch(q, k, v, out, metadata, N, G, scale, token_order)
+    return out
+
+
+def _check_inputs(q, k, v, metadata, global_strategy, num_warps, num_stages, scale):
+    """The reference's host checks of Q/K/V, metadata, tuning and scale
+    (paired_kernel.py:106-152); returns (N, G, scale)."""
     if q.ndim != 4 or k.shape != q.shape or v.shape != q.shape or any(x <= 0 for x in q.shape):
         raise ValueError("Equal nonempty B,H,N,D Q/K/V required")
     if q.shape[-1] not in (64, 128) or any(x.stride(-1) != 1 for x in (q, k, v)):
@@ -139,30 +193,4 @@ def paired_attention(
     scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
     if not math.isfinite(scale) or scale <= 0:
         raise ValueError("Positive finite scale required")
-    if out is not None:
-        if out.shape != q.shape or out.dtype != q.dtype or out.device != q.device or out.stride(-1) != 1:
-            raise ValueError("Output must match Q shape/dtype/device with contiguous D")
-        if any(s <= 0 for s in out.stride()) or not _non_overlapping_strides(out):
-            raise ValueError("Positive non-overlapping output strides required")
-        if torch.is_grad_enabled() and out.requires_grad:
-            raise ValueError("Inference output cannot require gradients")
-        begin, end = _tensor_byte_span(out)
-        for x in (q, k, v, metadata.kv_indices, metadata.kv_flags, metadata.kv_counts):
-            first, last = _tensor_byte_span(x)
-            if begin < last and first < end:
-                raise ValueError("Output cannot alias inputs or metadata")
-    else:
-        out = torch.empty_like(q)
-    if token_order is not None:
-        if (
-            not isinstance(token_order, torch.Tensor)
-            or token_order.dtype != torch.int32
-            or token_order.device != q.device
-            or token_order.shape != (N,)
-            or not token_order.is_contiguous()
-        ):
-            raise ValueError("token_order must be a contiguous int32 [N] tensor on the Q device")
-        if any(s % q.shape[-1] for x in (q, k, v) for s in x.stride()[:3]):
-            raise ValueError("token_order needs Q/K/V outer strides that are multiples of D")
-    _launch(q, k, v, out, metadata, N, G, scale, token_order)
-    return out
+    return N, G, scale

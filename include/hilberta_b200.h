@@ -18,6 +18,8 @@
  *                                  hilberta/sparse_kernel.py:155-166 (explicit_mask)
  *   hb_paired_fwd                  hilberta/paired_kernel.py:18-94 (_paired_fwd Triton kernel)
  *                                  launched by paired_kernel.py:97-205 (paired_attention)
+ *   hb_paired_fwd_allgather        the same kernel fused with the head-output gather
+ *                                  before to_out (hilberta/flux_adapter.py:328-339)
  */
 #ifndef HILBERTA_B200_H
 #define HILBERTA_B200_H
@@ -45,6 +47,7 @@ extern "C" {
 #define HB_DEV_TIMEOUT 1       /* a bounded barrier wait ran out; the kernel returned    */
 #define HB_DEV_BAD_COUNT 2     /* kv_counts entry outside [0, W]; clamped                */
 #define HB_DEV_BAD_BLOCK 4     /* kv_indices entry outside [0, N/64); its tile read zeros */
+#define HB_DEV_PEER_TIMEOUT 8  /* hb_paired_fwd_allgather: a peer's completion flag never came */
 
 /* Human-readable text for a status code (static storage). */
 const char* hb_status_string(int code);
@@ -161,6 +164,49 @@ int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const 
  * (hilberta/sampling_layout.py:88-116) touches HBM.  Rows are gathered with TMA
  * tile::gather4 (4 rows per instruction); Q/K/V outer strides must then be
  * multiples of D. */
+
+/* ---- attention fused with the all-gather of head outputs --------------- */
+/* Head-parallel ranks (one process per GPU, the heads split over the ranks;
+ * the gather the FLUX block does before to_out, hilberta/flux_adapter.py:328-339)
+ * need every rank's output heads on every rank.  Instead of the kernel followed
+ * by an all-gather, hb_paired_fwd_allgather writes each finished output row
+ * straight into every rank's full-head output over NVLink peer memory (plain
+ * stores into mappings from hb_ipc_open), so the transfer overlaps the math tile
+ * by tile.  When all of this rank's rows are stored it fences at system scope,
+ * sets its word in every rank's flag array to `epoch` and waits (bounded by
+ * timeout_ms; on expiry HB_DEV_PEER_TIMEOUT) until every rank has set its word
+ * in this rank's array: when the launch completes, all ranks' rows are in this
+ * rank's output.  The ranks must be on distinct GPUs.  A rank must not write a
+ * buffer a peer may still read: alternate two output buffers between calls (a
+ * rank reaches call e+1 only after every rank finished call e's kernel, hence
+ * everything it ordered before that kernel). */
+#define HB_MAX_RANKS 8
+typedef struct hb_peer_out_t {
+    int32_t n_ranks;               /* 1..HB_MAX_RANKS                                   */
+    int32_t rank;                  /* this rank: its word in every flag array            */
+    int32_t epoch;                 /* > 0, the same on all ranks, +1 per call            */
+    int32_t timeout_ms;            /* bound of the completion wait; 0 = 10000            */
+    void* out[HB_MAX_RANKS];       /* rank i's output at this rank's first head, strides
+                                      strides[9..11] (identical on all ranks)           */
+    int32_t* flags[HB_MAX_RANKS];  /* rank i's HB_MAX_RANKS flag words, zeroed once     */
+} hb_peer_out_t;
+/* Same arguments as hb_paired_fwd with `out` and `row_map` replaced by `peers`. */
+int hb_paired_fwd_allgather(const void* q, const void* k, const void* v, const int64_t* strides,
+                            int B, int H, int N, int D, int G, int W, int key_block_size,
+                            const int32_t* kv_indices, const int32_t* kv_flags,
+                            const int32_t* kv_counts, float scale_log2, int dtype,
+                            const hb_peer_out_t* peers, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* Peer mappings for hb_peer_out_t (CUDA IPC; no multicast objects).
+ * hb_ipc_export: handle (HB_IPC_HANDLE_BYTES) of the device allocation holding
+ * ptr, and ptr's byte offset in it.  hb_ipc_open (another process, same node):
+ * maps that allocation on the current device and returns base + offset;
+ * hb_ipc_close unmaps what hb_ipc_open returned (pass the same offset). */
+#define HB_IPC_HANDLE_BYTES 64
+int hb_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+int hb_ipc_open(const void* handle, uint64_t offset, void** ptr);
+int hb_ipc_close(void* ptr, uint64_t offset);
 
 /* ---- allocation-free variant of hb_paired_fwd --------------------------- */
 /* No counterpart in the reference: an addition for callers that must not

@@ -82,3 +82,30 @@ def test_build_entry_compiles_for_sm100a():
 
     assert "arch=compute_100a,code=sm_100a" in build.FLAGS
     assert build.OUT.exists()
+
+
+def test_allgather_argument_checks(lib):
+    """hb_paired_fwd_allgather rejects bad peer descriptions before touching the GPU."""
+    from hilberta_b200 import _lib
+
+    assert ctypes.sizeof(_lib.PeerOut) == 16 + 2 * 8 * _lib.HB_MAX_RANKS
+    fake = ctypes.c_void_p(1 << 20)
+    strides = (ctypes.c_int64 * 12)(*([256 * 128, 256 * 128, 128] * 4))
+    args = lambda peers: (fake, fake, fake, strides, 1, 1, 256, 128, 0, 1, 64, fake, fake, fake, 1.0, 1, peers, fake, 256, None)
+    assert lib.hb_paired_fwd_allgather(*args(None)) == _lib.HB_ERR_ARG
+
+    def peers(n=2, rank=0, epoch=1, timeout=0, misalign=0):
+        p = _lib.PeerOut()
+        p.n_ranks, p.rank, p.epoch, p.timeout_ms = n, rank, epoch, timeout
+        for i in range(max(0, min(n, _lib.HB_MAX_RANKS))):
+            p.out[i] = (1 << 22) * (i + 1) + (misalign if i else 0)
+            p.flags[i] = (1 << 21) * (i + 1)
+        return ctypes.byref(p)
+
+    for bad in (dict(n=0), dict(n=9), dict(rank=2), dict(rank=-1), dict(epoch=0), dict(timeout=-1), dict(misalign=8)):
+        assert lib.hb_paired_fwd_allgather(*args(peers(**bad))) == _lib.HB_ERR_ARG, bad
+    handle = ctypes.create_string_buffer(_lib.HB_IPC_HANDLE_BYTES)
+    off = ctypes.c_uint64()
+    assert lib.hb_ipc_export(None, handle, ctypes.byref(off)) == _lib.HB_ERR_ARG
+    assert lib.hb_ipc_open(None, 0, ctypes.byref(ctypes.c_void_p())) == _lib.HB_ERR_ARG
+    assert lib.hb_ipc_close(None, 0) == _lib.HB_ERR_ARG
