@@ -381,17 +381,22 @@ def nccl_side_timing(a, q, k, v, metas, flops, world, dev, hb, steps=5):
 
 def permutation_side_timing(a, q, k, v, metas, plan, dev, hb, steps=5):
     """Raster-order Q/K/V (the tensors as given, read as raster token order):
-    mean ms per call of the fused gather/scatter (``token_order``) against the
+    mean ms per call of the kernel reading/writing raster order in place
+    (``token_order``: 8x8-square boxes, and the general row-map gather) against the
     explicit path (index_select of Q/K/V into the plan's order, the kernel,
     scatter of O back; sampling_layout.py:88-116 per call)."""
-    from hilberta_b200.paired_kernel import token_order_map
+    from hilberta_b200.paired_kernel import raster_order, token_order_map
 
     rows = token_order_map(plan, dev)
+    squares = raster_order(plan, dev)
     idx = rows.long()
     out = torch.empty_like(q)
     kw = dict(global_strategy="triton", num_warps=8, num_stages=2)
 
     def fused(ph):
+        hb.paired_attention(q, k, v, metas[ph], out=out, token_order=squares, **kw)
+
+    def gathered(ph):
         hb.paired_attention(q, k, v, metas[ph], out=out, token_order=rows, **kw)
 
     def explicit(ph):
@@ -401,7 +406,8 @@ def permutation_side_timing(a, q, k, v, metas, plan, dev, hb, steps=5):
 
     res = {}
     with torch.inference_mode():
-        for name, fn in (("fused_ms_per_call", fused), ("explicit_ms_per_call", explicit)):
+        for name, fn in (("fused_ms_per_call", fused), ("gather4_ms_per_call", gathered),
+                         ("explicit_ms_per_call", explicit)):
             for ph in range(4):
                 fn(ph)
             torch.cuda.synchronize()
@@ -413,7 +419,8 @@ def permutation_side_timing(a, q, k, v, metas, plan, dev, hb, steps=5):
             e1.record()
             torch.cuda.synchronize()
             res[name] = round(e0.elapsed_time(e1) / (4 * steps), 4)
-    res["note"] = "Q/K/V in raster token order; fused = gather/scatter inside k_paired_fwd (tile::gather4)"
+    res["note"] = ("Q/K/V in raster token order; fused = one 8x8-square TMA box per key/query block "
+                   "(hb_paired_fwd_raster); gather4 = rows through a row map (tile::gather4)")
     return res
 
 

@@ -49,6 +49,7 @@ EXPORTS = (
     "hb_fwd_workspace_bytes_for",
     "hb_paired_fwd",
     "hb_paired_fwd_noalloc",
+    "hb_paired_fwd_raster",
     "hb_paired_fwd_allgather",
     "hb_ipc_export",
     "hb_ipc_open",
@@ -67,6 +68,12 @@ class PlanDims(ctypes.Structure):
         ("row_capacity", ctypes.c_int64),
         ("workspace_bytes", ctypes.c_int64),
     ]
+
+
+class RasterOrderC(ctypes.Structure):
+    """hb_raster_order_t: raster-order token layout (text prefix + image squares)."""
+
+    _fields_ = [("text_tokens", ctypes.c_int32), ("grid", ctypes.c_int32), ("block_origin", ctypes.c_void_p)]
 
 
 class PeerOut(ctypes.Structure):
@@ -100,6 +107,11 @@ _SIGS = {
         _I,
         [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I, _P,
          _P, ctypes.c_size_t, _P],
+    ),
+    "hb_paired_fwd_raster": (
+        _I,
+        [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I,
+         ctypes.POINTER(RasterOrderC), _P, ctypes.c_size_t, _P],
     ),
     "hb_paired_fwd_allgather": (
         _I,

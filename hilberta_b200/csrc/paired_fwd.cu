@@ -68,6 +68,13 @@ struct FwdParams {
     // gathered tensor maps are 2-D (D, rows); rs_* = (b, h, n) strides in rows.
     const int32_t* row_map;
     int64_t rs_q[3], rs_k[3], rs_v[3];
+    // MODE_SQUARES: tokens < 64*text_blocks are in physical order (text maps above,
+    // 64-row boxes); image block ib covers the 8x8 square whose top-left token is
+    // image row sq_origin[ib] (= y0*grid + x0), loaded through the 5-D maps
+    // (D, x, y, head, batch) based at the first image token.
+    CUtensorMap tmap_q_img, tmap_k_img, tmap_v_img;
+    int text_blocks, grid, img_blocks;
+    const int32_t* sq_origin;
     // Output rows go to n_out tensors (same strides o_s*): `out` alone, or every
     // rank's full-head output at this rank's first head (fused all-gather).  In
     // the latter mode (n_out > 1) the last CTA signals flags[i][rank] = epoch on
@@ -104,6 +111,13 @@ struct Cfg {
     static constexpr int TMEM_COLS = 256;
     static constexpr uint32_t S_COL0 = 0, O_COL = 128;
 };
+
+// Token layouts of Q/K/V/O (kernel template MODE):
+//   MODE_TILED    physical order, the layout the metadata indexes (4-D tiled maps)
+//   MODE_ROWS     any permutation: row row_map[p] holds physical token p (gather4)
+//   MODE_SQUARES  raster order of a text prefix + g x g image whose physical
+//                 64-token blocks are aligned 8x8 squares: one 5-D box per block
+constexpr int MODE_TILED = 0, MODE_ROWS = 1, MODE_SQUARES = 2;
 
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8 between rescales
 // One in POLY_EXP2_EVERY element pairs of a score row takes 2^x from ex2_poly2
@@ -218,9 +232,44 @@ __device__ __forceinline__ void gather_tile(const FwdParams& p, const CUtensorMa
     for (int s = 0; s < D / 64; s++) tma_gather4(dst + s * slab_bytes + 4 * lane * 128, map, bar, 64 * s, s0, s1, s2, s3);
 }
 
+// MODE_SQUARES: raster row of image block ib's first token, or -1 when the block
+// or its origin is invalid (out of range, or not the corner of an aligned 8x8 square).
+__device__ __forceinline__ int square_origin(const FwdParams& p, int ib) {
+    if (ib < 0 || ib >= p.img_blocks) return -1;
+    const int o = p.sq_origin[ib];
+    if (o < 0 || o >= p.grid * p.grid || ((o % p.grid) & 7) || ((o / p.grid) & 7)) return -1;
+    return o;
+}
+
+// MODE_SQUARES: one 64-token physical block into 64 rows of a swizzled tile (lane
+// 0 only): a text block through the 4-D map, an image block as one 8x8 box of
+// the 5-D map per 64-column slab.  A bad block reads fully out of bounds (zeros).
+template <int D>
+__device__ __forceinline__ void load_block_sq(const FwdParams& p, const CUtensorMap* text_map, const int32_t* perm,
+                                              const CUtensorMap* img_map, uint8_t* dst, int slab_bytes, uint64_t* bar,
+                                              int blk, int b, int h) {
+    if (blk >= 0 && blk < p.text_blocks) {
+        int c1, c2, c3;
+        tma_coords(perm, blk * 64, h, b, c1, c2, c3);
+#pragma unroll
+        for (int s = 0; s < D / 64; s++) tma_load_4d(dst + s * slab_bytes, text_map, bar, 64 * s, c1, c2, c3);
+        return;
+    }
+    const int o = square_origin(p, blk - p.text_blocks);
+    int x0 = 0, y0 = p.grid;  // y beyond the image: zero fill
+    if (o >= 0) {
+        x0 = o % p.grid;
+        y0 = o / p.grid;
+    } else {
+        atomicOr(&p.ws[2], HB_DEV_BAD_BLOCK);
+    }
+#pragma unroll
+    for (int s = 0; s < D / 64; s++) tma_load_5d(dst + s * slab_bytes, img_map, bar, 64 * s, x0, y0, h, b);
+}
+
 // Producer of one operand stream (warp-wide; lane 0 issues, every lane in gather
 // mode).  WHICH = 0: Q + K, 1: V.
-template <int D, int WHICH, bool GATHER>
+template <int D, int WHICH, int MODE>
 __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t* bar_item_full,
                          uint64_t* bar_item_empty, int* item_slot, uint64_t* bar_q_full, uint64_t* bar_q_empty,
                          uint64_t* bar_full, uint64_t* bar_empty, volatile int* abort_flag) {
@@ -254,10 +303,17 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
         const Item w = decode_item(p, item, WHICH == 0 && lane == 0);
         if (WHICH == 0) {
             if (!warp_wait(bar_q_empty, (it & 1) ^ 1, abort_flag, p.timeout)) break;
-            if constexpr (GATHER) {
+            if constexpr (MODE == MODE_ROWS) {
                 if (lane == 0) mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
                 __syncwarp();
                 gather_tile<D>(p, &p.tmap_q, p.rs_q, sQ, C::Q_SLAB, bar_q_full, w.qrow0, 128, w.b, w.h, false);
+            } else if constexpr (MODE == MODE_SQUARES) {
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
+                    for (int half = 0; half < 2; half++)  // query half = one physical block
+                        load_block_sq<D>(p, &p.tmap_q, p.perm_q, &p.tmap_q_img, sQ + half * 64 * 128, C::Q_SLAB,
+                                         bar_q_full, (w.qrow0 >> 6) + half, w.b, w.h);
+                }
             } else if (lane == 0) {
                 mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
                 int c1, c2, c3;
@@ -279,7 +335,7 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
                 break;
             }
             const bool bad = blk < 0 || blk >= p.nkb;
-            if constexpr (GATHER) {
+            if constexpr (MODE == MODE_ROWS) {
                 if (lane == 0) {
                     if (bad) atomicOr(&p.ws[2], HB_DEV_BAD_BLOCK);
                     mbar_arrive_expect_tx(&bar_full[st], C::KV_BYTES);
@@ -288,6 +344,13 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
                 // a bad block reads row -1: out of bounds, the TMA unit fills zeros
                 gather_tile<D>(p, tmap, rs, sKV + st * C::KV_BYTES, C::KV_SLAB, &bar_full[st], bad ? 0 : blk * 64, 64,
                                w.b, w.h, bad);
+            } else if constexpr (MODE == MODE_SQUARES) {
+                if (lane == 0) {
+                    if (bad) atomicOr(&p.ws[2], HB_DEV_BAD_BLOCK);
+                    mbar_arrive_expect_tx(&bar_full[st], C::KV_BYTES);
+                    load_block_sq<D>(p, tmap, perm, WHICH == 0 ? &p.tmap_k_img : &p.tmap_v_img,
+                                     sKV + st * C::KV_BYTES, C::KV_SLAB, &bar_full[st], bad ? -1 : blk, w.b, w.h);
+                }
             } else if (lane == 0) {
                 int rowc = blk * 64;
                 if (bad) {
@@ -396,7 +459,7 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
     }
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int MODE>
 __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_item_full, uint64_t* bar_item_empty,
                              int* item_slot, uint64_t* bar_s_full, uint64_t* bar_p_full, uint64_t* bar_o_done,
                              uint64_t* bar_o_empty, uint64_t* bar_wg, int* wg_flag, volatile int* abort_flag) {
@@ -511,8 +574,17 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
         if (!warp_wait(bar_o_done, gl & 1, abort_flag, p.timeout)) return;
         tc_fence_after();
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-        const int64_t ooff = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh +
-                             (int64_t)(p.row_map ? p.row_map[w.qrow0 + r] : w.qrow0 + r) * p.o_sn;
+        int orow = w.qrow0 + r;  // output token row of this thread's query
+        if constexpr (MODE == MODE_ROWS) orow = p.row_map[orow];
+        if constexpr (MODE == MODE_SQUARES) {
+            const int blk = orow >> 6;
+            if (blk >= p.text_blocks) {  // tile row r%64 of an image block = row-major position in its square
+                const int o = square_origin(p, blk - p.text_blocks);
+                orow = o < 0 ? -1 : 64 * p.text_blocks + o + ((orow & 63) >> 3) * p.grid + (orow & 7);
+            }
+        }
+        const bool row_ok = orow >= 0 && orow < p.N;  // a bad map entry drops the row, never stores out of range
+        const int64_t ooff = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh + (int64_t)(row_ok ? orow : 0) * p.o_sn;
         // every destination has the same address residue mod 16 (checked on the host)
         const bool vec = (reinterpret_cast<uintptr_t>(reinterpret_cast<T*>(p.outs[0]) + ooff) & 15) == 0;
         // Rows are written to this rank's output first (lane = row); with vector
@@ -524,7 +596,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             uint32_t packed[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) packed[i] = pack2<BF16>(vals[2 * i], vals[2 * i + 1]);
-            for (int d = 0; d < p.n_out; d++) {
+            for (int d = 0; d < p.n_out && row_ok; d++) {
                 if (d != p.rank && push) continue;
                 T* orow = reinterpret_cast<T*>(p.outs[d]) + ooff;
                 if (vec) {
@@ -676,7 +748,7 @@ __device__ __noinline__ void peer_complete(const FwdParams& p) {
     }
 }
 
-template <int D, bool BF16, bool GATHER>
+template <int D, bool BF16, int MODE>
 __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ FwdParams p) {
     using C = Cfg<D>;
     extern __shared__ uint8_t smem_raw[];
@@ -735,10 +807,10 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
     const uint32_t tmem = tmem_base_sh;
 
     if (warp == 0) {
-        producer<D, 0, GATHER>(p, sQ, sK, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_k_full,
+        producer<D, 0, MODE>(p, sQ, sK, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_k_full,
                        bar_k_empty, abort_flag);
     } else if (warp == 1) {
-        producer<D, 1, GATHER>(p, sQ, sV, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_v_full,
+        producer<D, 1, MODE>(p, sQ, sV, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_v_full,
                        bar_v_empty, abort_flag);
     } else if (warp == 2) {
         if (lane == 0)
@@ -746,7 +818,7 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
                                 &bar_q_empty, bar_k_full, bar_k_empty, bar_v_full, bar_v_empty, bar_s_full, bar_p_full,
                                 &bar_o_done, &bar_o_empty, &bar_drain, abort_flag);
     } else if (warp >= 4) {
-        softmax_role<D, BF16>(p, tmem, bar_item_full, bar_item_empty, item_slot, bar_s_full, bar_p_full, &bar_o_done,
+        softmax_role<D, BF16, MODE>(p, tmem, bar_item_full, bar_item_empty, item_slot, bar_s_full, bar_p_full, &bar_o_done,
                               &bar_o_empty, &bar_wg, &wg_flag, abort_flag);
     }
     tc_fence_before();
@@ -865,10 +937,36 @@ int make_tmap_rows(CUtensorMap* map, const void* base, bool bf16, int D, int N, 
     return r == CUDA_SUCCESS ? HB_OK : HB_ERR_TMA;
 }
 
+// MODE_SQUARES image map: the g x g image tokens that follow `text` tokens, as
+// (D, x, y, head, batch) with element strides (1, sn, g*sn, sh, sb) and a
+// {64, 8, 8, 1, 1} box, so one load gives an aligned 8x8 square as 64 swizzled
+// 128-byte rows in row-major square order.
+int make_tmap_img(CUtensorMap* map, const void* base, bool bf16, int D, int text, int g, int H, int B, int64_t sb,
+                  int64_t sh, int64_t sn) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return HB_ERR_CUDA;
+    const char* img = static_cast<const char*>(base) + (int64_t)text * sn * 2;
+    if (reinterpret_cast<uintptr_t>(img) & 15) return HB_ERR_TMA;
+    int64_t st[4] = {sn * 2, (int64_t)g * sn * 2, sh * 2, sb * 2};
+    const int64_t ext[4] = {g, g, H, B};
+    for (int i = 0; i < 4; i++) {
+        if (ext[i] == 1) st[i] = 16;  // never used for addressing
+        if (st[i] <= 0 || (st[i] & 15) || st[i] >= (int64_t(1) << 40)) return HB_ERR_TMA;
+    }
+    cuuint64_t gdim[5] = {(cuuint64_t)D, (cuuint64_t)g, (cuuint64_t)g, (cuuint64_t)H, (cuuint64_t)B};
+    cuuint64_t gstride[4] = {(cuuint64_t)st[0], (cuuint64_t)st[1], (cuuint64_t)st[2], (cuuint64_t)st[3]};
+    cuuint32_t box[5] = {64, 8, 8, 1, 1}, estride[5] = {1, 1, 1, 1, 1};
+    const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                           const_cast<char*>(img), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? HB_OK : HB_ERR_TMA;
+}
+
 struct DeviceInfo {
     int sms = 0;
     int clock_khz = 0;
-    bool configured[8] = {false, false, false, false, false, false, false, false};
+    bool configured[12] = {};
 };
 std::mutex g_mu;
 DeviceInfo g_dev[64];
@@ -887,11 +985,11 @@ int device_info(int dev, int* sms, int* clock_khz) {
     return HB_OK;
 }
 
-template <int D, bool BF16, bool GATHER>
+template <int D, bool BF16, int MODE>
 int launch(const FwdParams& p, int dev, cudaStream_t st) {
     using C = Cfg<D>;
-    auto kern = k_paired_fwd<D, BF16, GATHER>;
-    const int slot = (D == 128 ? 2 : 0) + (BF16 ? 1 : 0) + (GATHER ? 4 : 0);
+    auto kern = k_paired_fwd<D, BF16, MODE>;
+    const int slot = (D == 128 ? 2 : 0) + (BF16 ? 1 : 0) + 4 * MODE;
     int sms, rc;
     if ((rc = device_info(dev, &sms, nullptr))) return rc;
     {
@@ -963,8 +1061,15 @@ namespace {
 int paired_fwd(const void* q, const void* k, const void* v, void* out, const int64_t* strides, int B, int H, int N,
                int D, int G, int W, int key_block_size, const int32_t* kv_indices, const int32_t* kv_flags,
                const int32_t* kv_counts, float scale_log2, int dtype, const int32_t* row_map,
-               const hb_peer_out_t* peers, void* workspace, size_t workspace_bytes, void* stream_) {
+               const hb_raster_order_t* raster, const hb_peer_out_t* peers, void* workspace, size_t workspace_bytes,
+               void* stream_) {
     if (!q || !k || !v || !(out || peers) || !strides || !workspace) return HB_ERR_ARG;
+    if (raster) {
+        const int64_t T = raster->text_tokens, g = raster->grid;
+        if (T < 0 || T % 64 || g <= 0 || g % 8 || T + g * g != (int64_t)N || !raster->block_origin ||
+            (reinterpret_cast<uintptr_t>(raster->block_origin) & 3) || row_map || peers)
+            return HB_ERR_ARG;
+    }
     if (peers) {
         const int n = peers->n_ranks;
         if (n < 1 || n > HB_MAX_RANKS || peers->rank < 0 || peers->rank >= n || peers->epoch <= 0 ||
@@ -1002,6 +1107,18 @@ int paired_fwd(const void* q, const void* k, const void* v, void* out, const int
         if ((rc = make_tmap_rows(&p.tmap_q, q, bf16, D, N, H, B, strides[0], strides[1], strides[2], p.rs_q))) return rc;
         if ((rc = make_tmap_rows(&p.tmap_k, k, bf16, D, N, H, B, strides[3], strides[4], strides[5], p.rs_k))) return rc;
         if ((rc = make_tmap_rows(&p.tmap_v, v, bf16, D, N, H, B, strides[6], strides[7], strides[8], p.rs_v))) return rc;
+    } else if (raster) {
+        if ((rc = make_tmap(&p.tmap_q, q, bf16, D, N, H, B, strides[0], strides[1], strides[2], 64, p.perm_q))) return rc;
+        if ((rc = make_tmap(&p.tmap_k, k, bf16, D, N, H, B, strides[3], strides[4], strides[5], 64, p.perm_k))) return rc;
+        if ((rc = make_tmap(&p.tmap_v, v, bf16, D, N, H, B, strides[6], strides[7], strides[8], 64, p.perm_v))) return rc;
+        const int T = raster->text_tokens, g = raster->grid;
+        if ((rc = make_tmap_img(&p.tmap_q_img, q, bf16, D, T, g, H, B, strides[0], strides[1], strides[2]))) return rc;
+        if ((rc = make_tmap_img(&p.tmap_k_img, k, bf16, D, T, g, H, B, strides[3], strides[4], strides[5]))) return rc;
+        if ((rc = make_tmap_img(&p.tmap_v_img, v, bf16, D, T, g, H, B, strides[6], strides[7], strides[8]))) return rc;
+        p.text_blocks = T / 64;
+        p.grid = g;
+        p.img_blocks = g * g / 64;
+        p.sq_origin = raster->block_origin;
     } else {
         if ((rc = make_tmap(&p.tmap_q, q, bf16, D, N, H, B, strides[0], strides[1], strides[2], 128, p.perm_q))) return rc;
         if ((rc = make_tmap(&p.tmap_k, k, bf16, D, N, H, B, strides[3], strides[4], strides[5], 64, p.perm_k))) return rc;
@@ -1065,11 +1182,16 @@ int paired_fwd(const void* q, const void* k, const void* v, void* out, const int
     p.timeout = 2000000000ll;
     cudaStream_t st = (cudaStream_t)stream_;
     if (row_map) {
-        if (D == 128) return bf16 ? launch<128, true, true>(p, dev, st) : launch<128, false, true>(p, dev, st);
-        return bf16 ? launch<64, true, true>(p, dev, st) : launch<64, false, true>(p, dev, st);
+        if (D == 128) return bf16 ? launch<128, true, MODE_ROWS>(p, dev, st) : launch<128, false, MODE_ROWS>(p, dev, st);
+        return bf16 ? launch<64, true, MODE_ROWS>(p, dev, st) : launch<64, false, MODE_ROWS>(p, dev, st);
     }
-    if (D == 128) return bf16 ? launch<128, true, false>(p, dev, st) : launch<128, false, false>(p, dev, st);
-    return bf16 ? launch<64, true, false>(p, dev, st) : launch<64, false, false>(p, dev, st);
+    if (raster) {
+        if (D == 128)
+            return bf16 ? launch<128, true, MODE_SQUARES>(p, dev, st) : launch<128, false, MODE_SQUARES>(p, dev, st);
+        return bf16 ? launch<64, true, MODE_SQUARES>(p, dev, st) : launch<64, false, MODE_SQUARES>(p, dev, st);
+    }
+    if (D == 128) return bf16 ? launch<128, true, MODE_TILED>(p, dev, st) : launch<128, false, MODE_TILED>(p, dev, st);
+    return bf16 ? launch<64, true, MODE_TILED>(p, dev, st) : launch<64, false, MODE_TILED>(p, dev, st);
 }
 }  // namespace
 }  // namespace hb
@@ -1080,7 +1202,17 @@ extern "C" int hb_paired_fwd(const void* q, const void* k, const void* v, void* 
                              const int32_t* row_map, void* workspace, size_t workspace_bytes, void* stream) {
     if (!out) return HB_ERR_ARG;
     return paired_fwd(q, k, v, out, strides, B, H, N, D, G, W, key_block_size, kv_indices, kv_flags, kv_counts,
-                      scale_log2, dtype, row_map, nullptr, workspace, workspace_bytes, stream);
+                      scale_log2, dtype, row_map, nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int hb_paired_fwd_raster(const void* q, const void* k, const void* v, void* out, const int64_t* strides,
+                                    int B, int H, int N, int D, int G, int W, int key_block_size,
+                                    const int32_t* kv_indices, const int32_t* kv_flags, const int32_t* kv_counts,
+                                    float scale_log2, int dtype, const hb_raster_order_t* order, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    if (!out || !order) return HB_ERR_ARG;
+    return paired_fwd(q, k, v, out, strides, B, H, N, D, G, W, key_block_size, kv_indices, kv_flags, kv_counts,
+                      scale_log2, dtype, nullptr, order, nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int hb_paired_fwd_allgather(const void* q, const void* k, const void* v, const int64_t* strides, int B,
@@ -1090,7 +1222,7 @@ extern "C" int hb_paired_fwd_allgather(const void* q, const void* k, const void*
                                        size_t workspace_bytes, void* stream) {
     if (!peers) return HB_ERR_ARG;
     return paired_fwd(q, k, v, nullptr, strides, B, H, N, D, G, W, key_block_size, kv_indices, kv_flags, kv_counts,
-                      scale_log2, dtype, nullptr, peers, workspace, workspace_bytes, stream);
+                      scale_log2, dtype, nullptr, nullptr, peers, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------

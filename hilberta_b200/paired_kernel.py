@@ -55,7 +55,7 @@ def device_status(device=None, *, clear=True) -> int:
     return bits
 
 
-def _launch(q, k, v, out, metadata, N, G, scale, row_map=None):
+def _launch(q, k, v, out, metadata, N, G, scale, row_map=None, raster=None):
     """The one native call of the attention path."""
     dev = q.device
     stream = torch.cuda.current_stream(dev)
@@ -63,13 +63,18 @@ def _launch(q, k, v, out, metadata, N, G, scale, row_map=None):
     lib = _lib.lib()
     ws = _workspace(dev, stream.cuda_stream, lib.hb_fwd_workspace_bytes_for(B, H, N, G, D))
     strides = (ctypes.c_int64 * 12)(*q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *out.stride()[:3])
-    rc = lib.hb_paired_fwd(
+    common = (
         _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), strides, B, H, N, D, G,
         int(metadata.kv_indices.shape[1]), int(metadata.key_block_size),
         _lib.ptr(metadata.kv_indices), _lib.ptr(metadata.kv_flags), _lib.ptr(metadata.kv_counts),
-        float(scale * LOG2E), 1 if q.dtype == torch.bfloat16 else 0, _lib.ptr(row_map), _lib.ptr(ws),
-        ws.numel() * 4, ctypes.c_void_p(stream.cuda_stream),
+        float(scale * LOG2E), 1 if q.dtype == torch.bfloat16 else 0,
     )
+    tail = (_lib.ptr(ws), ws.numel() * 4, ctypes.c_void_p(stream.cuda_stream))
+    if raster is not None:
+        order = _lib.RasterOrderC(raster.text_tokens, raster.grid, raster.block_origin.data_ptr())
+        rc = lib.hb_paired_fwd_raster(*common, ctypes.byref(order), *tail)
+    else:
+        rc = lib.hb_paired_fwd(*common, _lib.ptr(row_map), *tail)
     if rc == _lib.HB_ERR_TMA:
         raise ValueError("Q/K/V need 16-byte aligned base pointers and strides for TMA tiles")
     if rc == _lib.HB_ERR_UNSUPPORTED:
@@ -98,6 +103,49 @@ def _launch_allgather(q, k, v, full, metadata, N, G, scale, peers):
     _lib.check(rc, "hb_paired_fwd_allgather")
 
 
+class RasterOrder:
+    """Raster token layout of a plan for ``paired_attention(token_order=...)``:
+    ``text_tokens`` text tokens, then the ``grid x grid`` image in row-major
+    order.  ``block_origin`` (int32, on the device) holds, for each physical
+    64-token image block, the image row y0*grid + x0 of the aligned 8x8 square it
+    covers; the kernel loads each block as one square and writes its output rows
+    back into it."""
+
+    def __init__(self, text_tokens: int, grid: int, block_origin: torch.Tensor):
+        self.text_tokens, self.grid, self.block_origin = int(text_tokens), int(grid), block_origin
+
+    @property
+    def tokens(self) -> int:
+        return self.text_tokens + self.grid * self.grid
+
+    def rows(self) -> torch.Tensor:
+        """The equivalent row map for the kernel's token order: physical token p
+        of block b at row-major position i of its square -> raster row."""
+        o = self.block_origin.to(torch.int64)
+        i = torch.arange(64, device=o.device)
+        img = self.text_tokens + o[:, None] + (i // 8)[None, :] * self.grid + (i % 8)[None, :]
+        return torch.cat([torch.arange(self.text_tokens, device=o.device), img.reshape(-1)]).to(torch.int32)
+
+
+def raster_order(plan, device) -> RasterOrder:
+    """RasterOrder of a plan; raises ValueError when a physical image block is not
+    an aligned 8x8 square of the image (every plan of build_plan / bridge_k_plan
+    has this property: the Hilbert walk fills aligned squares 64 cells at a time)."""
+    t = int(plan.text_tokens)
+    order = torch.as_tensor(plan.image_order).to(torch.int64).cpu()
+    g = int(round(order.numel() ** 0.5))
+    if g * g != order.numel() or g % 8 or t % 64:
+        raise ValueError("raster_order needs a square image with a side divisible by 8 and a 64-aligned text prefix")
+    blocks = order.view(-1, 64)
+    y, x = blocks // g, blocks % g
+    x0, y0 = x.min(dim=1).values, y.min(dim=1).values
+    i = torch.arange(64)
+    want = (y0[:, None] + i // 8) * g + x0[:, None] + i % 8
+    if (x0 % 8).any() or (y0 % 8).any() or not torch.equal(blocks.sort(dim=1).values, want):
+        raise ValueError("plan image blocks are not aligned 8x8 squares; use token_order_map")
+    return RasterOrder(t, g, (y0 * g + x0).to(torch.int32).to(device).contiguous())
+
+
 def token_order_map(plan, device) -> torch.Tensor:
     """Physical -> raster row map of a plan for ``paired_attention(token_order=...)``:
     text rows first (identity), then ``text_tokens + image_order`` (plan.py:147)."""
@@ -116,11 +164,15 @@ def paired_attention(
     e.g. BNHD storage viewed as BHND), fp16/bf16.  Returns ``out`` (allocated
     with ``torch.empty_like(q)`` when not given, preserving q's storage order).
 
-    ``token_order`` (extension, keyword only): int32 CUDA tensor [N] mapping each
-    physical token of the metadata's layout to its row in q/k/v/out, e.g.
-    ``token_order_map(plan, device)`` for tensors kept in raster order; the
-    kernel then gathers rows while loading and scatters output rows, replacing
-    the reference's separate reorder pass (sampling_layout.py:88-116).
+    ``token_order`` (extension, keyword only), for q/k/v/out kept in raster token
+    order instead of the metadata's physical order, replacing the reference's
+    separate reorder passes (sampling_layout.py:88-116):
+
+    * ``raster_order(plan, device)`` (fast): each 64-token block is loaded as one
+      aligned 8x8 image square and its output rows are written back into it;
+    * an int32 CUDA tensor [N] mapping each physical token to its row, e.g.
+      ``token_order_map(plan, device)`` (any permutation; rows are gathered four
+      at a time, Q/K/V outer strides must be multiples of D).
     """
     N, G, scale = _check_inputs(q, k, v, metadata, global_strategy, num_warps, num_stages, scale)
     if out is not None:
@@ -137,6 +189,14 @@ def paired_attention(
                 raise ValueError("Output cannot alias inputs or metadata")
     else:
         out = torch.empty_like(q)
+    if isinstance(token_order, RasterOrder):
+        bo = token_order.block_origin
+        if token_order.tokens != N or bo.dtype != torch.int32 or bo.device != q.device or not bo.is_contiguous():
+            raise ValueError("token_order must describe N tokens with int32 block origins on the Q device")
+        if bo.shape != (token_order.grid * token_order.grid // 64,):
+            raise ValueError("token_order block_origin needs one entry per 64-token image block")
+        _launch(q, k, v, out, metadata, N, G, scale, raster=token_order)
+        return out
     if token_order is not None:
         if (
             not isinstance(token_order, torch.Tensor)

@@ -18,6 +18,8 @@
  *                                  hilberta/sparse_kernel.py:155-166 (explicit_mask)
  *   hb_paired_fwd                  hilberta/paired_kernel.py:18-94 (_paired_fwd Triton kernel)
  *                                  launched by paired_kernel.py:97-205 (paired_attention)
+ *   hb_paired_fwd_raster           the same kernel on raster-order tensors, replacing the
+ *                                  reorder passes of hilberta/sampling_layout.py:88-116
  *   hb_paired_fwd_allgather        the same kernel fused with the head-output gather
  *                                  before to_out (hilberta/flux_adapter.py:328-339)
  */
@@ -164,6 +166,33 @@ int hb_paired_fwd(const void* q, const void* k, const void* v, void* out, const 
  * (hilberta/sampling_layout.py:88-116) touches HBM.  Rows are gathered with TMA
  * tile::gather4 (4 rows per instruction); Q/K/V outer strides must then be
  * multiples of D. */
+
+/* ---- raster-order tensors, block by block ------------------------------- */
+/* Same computation as hb_paired_fwd for Q/K/V/O kept in raster token order:
+ * the first text_tokens tokens in physical order, then a grid x grid image in
+ * row-major order (N = text_tokens + grid^2).  The plan's physical image order
+ * (hilberta/plan.py:133-150, :192) walks each 64-token block over one aligned
+ * 8x8 square of the image, so block b is loaded as one 8x8 box per tile and
+ * its output rows are written back into the same square — the reference's
+ * reorder passes before and after the transformer (sampling_layout.py:88-116)
+ * are not needed.  block_origin: device int32 [grid^2 / 64], the image row
+ * (y0 * grid + x0) of the square physical image block b covers.  A block
+ * whose origin is not the corner of an aligned square reads zeros, its rows
+ * are not written, and HB_DEV_BAD_BLOCK is set.  Within a block, keys and
+ * queries are taken in the square's row-major order, so results equal
+ * hb_paired_fwd's on tensors permuted to that order (the same values up to
+ * the order of fp32 sums otherwise). */
+typedef struct hb_raster_order_t {
+    int32_t text_tokens;          /* multiple of 64                              */
+    int32_t grid;                 /* image side, multiple of 8                   */
+    const int32_t* block_origin;  /* device, [grid * grid / 64]                  */
+} hb_raster_order_t;
+int hb_paired_fwd_raster(const void* q, const void* k, const void* v, void* out,
+                         const int64_t* strides, int B, int H, int N, int D, int G, int W,
+                         int key_block_size, const int32_t* kv_indices, const int32_t* kv_flags,
+                         const int32_t* kv_counts, float scale_log2, int dtype,
+                         const hb_raster_order_t* order, void* workspace, size_t workspace_bytes,
+                         void* stream);
 
 /* ---- attention fused with the all-gather of head outputs --------------- */
 /* Head-parallel ranks (one process per GPU, the heads split over the ranks;

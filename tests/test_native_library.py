@@ -109,3 +109,23 @@ def test_allgather_argument_checks(lib):
     assert lib.hb_ipc_export(None, handle, ctypes.byref(off)) == _lib.HB_ERR_ARG
     assert lib.hb_ipc_open(None, 0, ctypes.byref(ctypes.c_void_p())) == _lib.HB_ERR_ARG
     assert lib.hb_ipc_close(None, 0) == _lib.HB_ERR_ARG
+
+
+def test_raster_argument_checks(lib):
+    """hb_paired_fwd_raster rejects inconsistent layouts before touching the GPU."""
+    from hilberta_b200 import _lib
+
+    fake = ctypes.c_void_p(1 << 20)
+    strides = (ctypes.c_int64 * 12)(*([768 * 128, 768 * 128, 128] * 4))
+
+    def call(order):
+        ref = ctypes.byref(order) if order is not None else None
+        return lib.hb_paired_fwd_raster(fake, fake, fake, fake, strides, 1, 1, 768, 128, 0, 1, 64, fake, fake, fake,
+                                        1.0, 1, ref, fake, 256, None)
+
+    assert call(None) == _lib.HB_ERR_ARG
+    ok = 1 << 20
+    for t, g, origin in ((500, 16, ok), (512, 12, ok), (448, 16, ok), (512, 16, 0), (512, 16, ok + 2)):
+        assert call(_lib.RasterOrderC(t, g, origin)) == _lib.HB_ERR_ARG, (t, g, origin)
+    # 512 + 16*16 = 768 tokens is consistent: the layout checks pass and the call fails only for want of a GPU
+    assert call(_lib.RasterOrderC(512, 16, ok)) in (_lib.HB_ERR_CUDA, _lib.HB_OK)
