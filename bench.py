@@ -252,6 +252,7 @@ def run_native(a):
     value = sum(flops) * a.steps / (total_ms * 1e-3) / 1e12
 
     perm = permutation_side_timing(a, q, k, v, metas, plan, dev, hb) if world == 1 else None
+    prep_t = prep_side_timing(plan, H, dev) if world == 1 else None
     nccl = nccl_side_timing(a, q, k, v, metas, flops, world, dev, hb) if world > 1 else None
 
     e2e = None
@@ -311,6 +312,10 @@ def run_native(a):
     }
     if perm is not None:
         line["token_order"] = perm
+    if prep_t is not None:
+        prep_t["frac_hbm"] = round(prep_t["achieved_gbs"] / hbm, 4)
+        prep_t["peak_gbs"] = hbm
+        line["prep"] = prep_t
     if world > 1:
         # fused compute + collective: the target is the slower of the tensor time
         # and this GPU's share of the NVLink traffic (its rows to P-1 peers)
@@ -333,6 +338,62 @@ def run_native(a):
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def prep_side_timing(plan, H, dev, steps=10, D=128):
+    """The processor's Q/K/V preparation at this config (hilberta/flux_adapter.py:
+    280-298): hb_norm_rope_pack for Q, K, V against the same steps as eager torch
+    ops; HBM bytes = the six projections read + Q/K/V written + cos/sin read by
+    the Q and K passes."""
+    from hilberta_b200 import prep
+
+    T, N = plan.text_tokens, plan.total_tokens
+    n = N - T
+    g = torch.Generator(device="cpu").manual_seed(11)
+    proj = [torch.randn(1, T if i < 3 else n, H * D, generator=g).to(torch.bfloat16).to(dev) for i in range(6)]
+    w = [torch.ones(D, dtype=torch.bfloat16, device=dev) for _ in range(4)]
+    ang = torch.rand(N, D // 2, generator=g) * 6.28
+    cos = torch.cos(ang).repeat_interleave(2, dim=1).to(dev)
+    sin = torch.sin(ang).repeat_interleave(2, dim=1).to(dev)
+
+    def fused():
+        prep.prepare_qkv(*proj, heads=H, norm_q=w[0], norm_k=w[1], norm_added_q=w[2], norm_added_k=w[3],
+                         rotary=(cos, sin))
+
+    def eager():
+        def norm(x, wt):
+            x = x.unflatten(-1, (H, -1))
+            y = (x * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype)
+            return y * wt
+
+        def rope(x):
+            re, im = x.reshape(*x.shape[:-1], -1, 2).unbind(-1)
+            rot = torch.stack([-im, re], dim=-1).flatten(3)
+            return (x.float() * cos[None, :, None] + rot.float() * sin[None, :, None]).to(x.dtype)
+
+        qq = rope(torch.cat([norm(proj[0], w[2]), norm(proj[3], w[0])], dim=1))
+        kk = rope(torch.cat([norm(proj[1], w[3]), norm(proj[4], w[1])], dim=1))
+        vv = torch.cat([proj[2].unflatten(-1, (H, -1)), proj[5].unflatten(-1, (H, -1))], dim=1)
+        return qq, kk, vv
+
+    res = {}
+    with torch.inference_mode():
+        for name, fn in (("ms", fused), ("eager_ms", eager)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            res[name] = round(e0.elapsed_time(e1) / steps, 4)
+    nbytes = 2 * (3 * N * H * D * 2) + 2 * (2 * N * D * 4)
+    res["bytes"] = nbytes
+    res["achieved_gbs"] = round(nbytes / (res["ms"] * 1e-3) / 1e9, 1)
+    res["note"] = "Q,K,V: per-head RMSNorm + text/image cat + rotary + [B,S,H,D] pack (hb_norm_rope_pack) vs eager torch"
+    return res
 
 
 def nccl_side_timing(a, q, k, v, metas, flops, world, dev, hb, steps=5):

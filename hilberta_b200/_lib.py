@@ -50,6 +50,7 @@ EXPORTS = (
     "hb_paired_fwd",
     "hb_paired_fwd_noalloc",
     "hb_paired_fwd_raster",
+    "hb_norm_rope_pack",
     "hb_paired_fwd_allgather",
     "hb_ipc_export",
     "hb_ipc_open",
@@ -112,6 +113,11 @@ _SIGS = {
         _I,
         [_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, ctypes.c_float, _I,
          ctypes.POINTER(RasterOrderC), _P, ctypes.c_size_t, _P],
+    ),
+    "hb_norm_rope_pack": (
+        _I,
+        [_P, _I64, _I64, _P, _I64, _I64, _I, _I, _I, _I, _I, _P, _P, ctypes.c_float, _P, _P, _P, _P, _I64, _I64,
+         _I64, _I, _P, _P],
     ),
     "hb_paired_fwd_allgather": (
         _I,

@@ -18,6 +18,8 @@
  *                                  hilberta/sparse_kernel.py:155-166 (explicit_mask)
  *   hb_paired_fwd                  hilberta/paired_kernel.py:18-94 (_paired_fwd Triton kernel)
  *                                  launched by paired_kernel.py:97-205 (paired_attention)
+ *   hb_norm_rope_pack              hilberta/flux_adapter.py:280-298 (norm_q/norm_k,
+ *                                  text+image cat, apply_rotary_emb, BNHD views)
  *   hb_paired_fwd_raster           the same kernel on raster-order tensors, replacing the
  *                                  reorder passes of hilberta/sampling_layout.py:88-116
  *   hb_paired_fwd_allgather        the same kernel fused with the head-output gather
@@ -236,6 +238,31 @@ int hb_paired_fwd_allgather(const void* q, const void* k, const void* v, const i
 int hb_ipc_export(const void* ptr, void* handle, uint64_t* offset);
 int hb_ipc_open(const void* handle, uint64_t offset, void** ptr);
 int hb_ipc_close(void* ptr, uint64_t offset);
+
+/* ---- Q/K/V preparation before the attention ----------------------------- */
+/* The FLUX processor's steps between the projections and the attention
+ * (hilberta/flux_adapter.py:280-298), for one of Q, K or V, in one pass over
+ * HBM: split into H heads of D, RMS-normalise each (token, head) row over D with
+ * a learned weight (w_txt for the text stream, w_img for the image stream; both
+ * NULL: no normalisation, as for V), put the T text tokens first, rotate pairs
+ * (2i, 2i+1) by the rotary embedding (cos/sin NULL: no rotation) and write
+ * out[b][s][h][:] (element strides o_sb, o_sn, o_sh; [B, S, H, D] storage is
+ * what the attention reads in place through [B, H, S, D] views).
+ *   txt [B][T][H*D], img [B][n][H*D]: 16-bit (dtype 0 fp16, 1 bf16) with element
+ *   strides (txt_sb, txt_sn), (img_sb, img_sn); weights [D] in the same dtype;
+ *   cos/sin fp32 [T+n][D] indexed by OUTPUT token.  image_rows (optional, device
+ *   int32 [n]): image token i is written to token T + image_rows[i] (e.g. the
+ *   plan's inverse order, to produce the physical layout); an entry outside
+ *   [0, n) drops that row and sets HB_DEV_BAD_BLOCK in *status (optional).
+ * The rounding follows the ops it replaces (diffusers 0.36 RMSNorm and
+ * apply_rotary_emb): fp32 mean of squares, round to 16 bits after x*rsqrt and
+ * after *weight, rotation as separately rounded fp32 products and sum.
+ * Pointers 16-byte aligned, strides multiples of 8 elements; D 64 or 128. */
+int hb_norm_rope_pack(const void* txt, int64_t txt_sb, int64_t txt_sn, const void* img,
+                      int64_t img_sb, int64_t img_sn, int B, int T, int n, int H, int D,
+                      const void* w_txt, const void* w_img, float eps, const float* cos,
+                      const float* sin, const int32_t* image_rows, void* out, int64_t o_sb,
+                      int64_t o_sn, int64_t o_sh, int dtype, int32_t* status, void* stream);
 
 /* ---- allocation-free variant of hb_paired_fwd --------------------------- */
 /* No counterpart in the reference: an addition for callers that must not

@@ -129,3 +129,26 @@ def test_raster_argument_checks(lib):
         assert call(_lib.RasterOrderC(t, g, origin)) == _lib.HB_ERR_ARG, (t, g, origin)
     # 512 + 16*16 = 768 tokens is consistent: the layout checks pass and the call fails only for want of a GPU
     assert call(_lib.RasterOrderC(512, 16, ok)) in (_lib.HB_ERR_CUDA, _lib.HB_OK)
+
+
+def test_norm_rope_pack_argument_checks(lib):
+    """hb_norm_rope_pack validates shapes, pairs of optional arguments and
+    alignment on the host (no GPU touched on these paths)."""
+    from hilberta_b200 import _lib
+
+    f = ctypes.c_void_p(1 << 20)
+
+    def call(txt=f, img=f, T=16, n=64, H=2, D=128, wt=None, wi=None, eps=1e-6, cos=None, sin=None, out=f, sn=256,
+             dtype=1):
+        return lib.hb_norm_rope_pack(txt, 16 * sn, sn, img, 64 * sn, sn, 1, T, n, H, D, wt, wi, eps, cos, sin, None,
+                                     out, 80 * sn, sn, 128, dtype, None, None)
+
+    assert call(out=None) == _lib.HB_ERR_ARG
+    assert call(txt=None) == _lib.HB_ERR_ARG  # T > 0 needs text rows
+    assert call(wt=f) == _lib.HB_ERR_ARG  # one weight without the other
+    assert call(cos=f) == _lib.HB_ERR_ARG  # cos without sin
+    assert call(eps=-1.0) == _lib.HB_ERR_ARG
+    assert call(D=96) == _lib.HB_ERR_UNSUPPORTED
+    assert call(dtype=2) == _lib.HB_ERR_UNSUPPORTED
+    assert call(img=ctypes.c_void_p((1 << 20) + 8)) == _lib.HB_ERR_ALIGN
+    assert call(sn=260) == _lib.HB_ERR_ALIGN  # row stride not a multiple of 8 elements
