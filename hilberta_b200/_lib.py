@@ -31,6 +31,7 @@ HB_DEV_TIMEOUT = 1
 HB_DEV_BAD_COUNT = 2
 HB_DEV_BAD_BLOCK = 4
 HB_DEV_PEER_TIMEOUT = 8
+HB_DEV_SMEM_ALIGN = 16
 
 HB_MAX_RANKS = 8
 HB_IPC_HANDLE_BYTES = 64

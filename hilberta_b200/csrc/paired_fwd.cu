@@ -105,9 +105,22 @@ struct Cfg {
     static constexpr int KV_SLAB = 64 * 128;       // 64 rows x 128 B
     static constexpr int Q_BYTES = Q_SLAB * SLABS;
     static constexpr int KV_BYTES = KV_SLAB * SLABS;
-    static constexpr int KS = 2;  // K stages
+    static constexpr int KS = 3;  // K stages: a K tile is issued while the two before it are consumed
     static constexpr int VS = 2;  // V stages
-    static constexpr int SMEM = Q_BYTES + (KS + VS) * KV_BYTES + 1024;
+    // Mbarriers and slots live after the tiles in the dynamic region (no static
+    // shared memory, so the region starts 1024-byte aligned with no padding:
+    // two CTAs with three K stages fit in an SM's 228 KB).
+    struct Ctl {
+        uint64_t q_full, q_empty, o_done, o_empty, drain, wg;
+        uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
+        uint64_t s_full[2], p_full[2], item_full[2], item_empty[2];
+        int item_slot[2];
+        uint32_t tmem_base;
+        int abort;
+        int wg_flag;
+    };
+    static constexpr int CTL_OFF = Q_BYTES + (KS + VS) * KV_BYTES;
+    static constexpr int SMEM = CTL_OFF + (int)((sizeof(Ctl) + 15) / 16 * 16);
     static constexpr int TMEM_COLS = 256;
     static constexpr uint32_t S_COL0 = 0, O_COL = 128;
 };
@@ -247,12 +260,13 @@ __device__ __forceinline__ int square_origin(const FwdParams& p, int ib) {
 template <int D>
 __device__ __forceinline__ void load_block_sq(const FwdParams& p, const CUtensorMap* text_map, const int32_t* perm,
                                               const CUtensorMap* img_map, uint8_t* dst, int slab_bytes, uint64_t* bar,
-                                              int blk, int b, int h) {
+                                              int blk, int b, int h, uint64_t policy) {
     if (blk >= 0 && blk < p.text_blocks) {
         int c1, c2, c3;
         tma_coords(perm, blk * 64, h, b, c1, c2, c3);
 #pragma unroll
-        for (int s = 0; s < D / 64; s++) tma_load_4d(dst + s * slab_bytes, text_map, bar, 64 * s, c1, c2, c3);
+        for (int s = 0; s < D / 64; s++)
+            tma_load_4d_hint(dst + s * slab_bytes, text_map, bar, 64 * s, c1, c2, c3, policy);
         return;
     }
     const int o = square_origin(p, blk - p.text_blocks);
@@ -264,7 +278,8 @@ __device__ __forceinline__ void load_block_sq(const FwdParams& p, const CUtensor
         atomicOr(&p.ws[2], HB_DEV_BAD_BLOCK);
     }
 #pragma unroll
-    for (int s = 0; s < D / 64; s++) tma_load_5d(dst + s * slab_bytes, img_map, bar, 64 * s, x0, y0, h, b);
+    for (int s = 0; s < D / 64; s++)
+        tma_load_5d_hint(dst + s * slab_bytes, img_map, bar, 64 * s, x0, y0, h, b, policy);
 }
 
 // Producer of one operand stream (warp-wide; lane 0 issues, every lane in gather
@@ -281,6 +296,11 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
     const int64_t* rs = WHICH == 0 ? p.rs_k : p.rs_v;
     uint32_t gx = 0;  // loads issued over this CTA's lifetime
     bool ok = true;
+    // L2 priorities: K/V tiles are re-read by every pair-row that lists them,
+    // Q tiles are read once (as are the output rows): keep the former, let the
+    // latter go first.
+    const uint64_t pol_kv = l2_policy_evict_last();
+    const uint64_t pol_q = l2_policy_evict_first();
     for (int it = 0; ok; it++) {
         const int slot = it & 1;
         int item;
@@ -312,14 +332,15 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
                     mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
                     for (int half = 0; half < 2; half++)  // query half = one physical block
                         load_block_sq<D>(p, &p.tmap_q, p.perm_q, &p.tmap_q_img, sQ + half * 64 * 128, C::Q_SLAB,
-                                         bar_q_full, (w.qrow0 >> 6) + half, w.b, w.h);
+                                         bar_q_full, (w.qrow0 >> 6) + half, w.b, w.h, pol_q);
                 }
             } else if (lane == 0) {
                 mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
                 int c1, c2, c3;
                 tma_coords(p.perm_q, w.qrow0, w.h, w.b, c1, c2, c3);
 #pragma unroll
-                for (int s = 0; s < C::SLABS; s++) tma_load_4d(sQ + s * C::Q_SLAB, &p.tmap_q, bar_q_full, 64 * s, c1, c2, c3);
+                for (int s = 0; s < C::SLABS; s++)
+                    tma_load_4d_hint(sQ + s * C::Q_SLAB, &p.tmap_q, bar_q_full, 64 * s, c1, c2, c3, pol_q);
             }
         }
         int chunk = 0;
@@ -349,7 +370,8 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
                     if (bad) atomicOr(&p.ws[2], HB_DEV_BAD_BLOCK);
                     mbar_arrive_expect_tx(&bar_full[st], C::KV_BYTES);
                     load_block_sq<D>(p, tmap, perm, WHICH == 0 ? &p.tmap_k_img : &p.tmap_v_img,
-                                     sKV + st * C::KV_BYTES, C::KV_SLAB, &bar_full[st], bad ? -1 : blk, w.b, w.h);
+                                     sKV + st * C::KV_BYTES, C::KV_SLAB, &bar_full[st], bad ? -1 : blk, w.b, w.h,
+                                     pol_kv);
                 }
             } else if (lane == 0) {
                 int rowc = blk * 64;
@@ -362,7 +384,8 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
                 tma_coords(perm, rowc, w.h, w.b, c1, c2, c3);
 #pragma unroll
                 for (int s = 0; s < C::SLABS; s++)
-                    tma_load_4d(sKV + st * C::KV_BYTES + s * C::KV_SLAB, tmap, &bar_full[st], 64 * s, c1, c2, c3);
+                    tma_load_4d_hint(sKV + st * C::KV_BYTES + s * C::KV_SLAB, tmap, &bar_full[st], 64 * s, c1, c2, c3,
+                                     pol_kv);
             }
         }
     }
@@ -400,56 +423,71 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
         const Item w = decode_item(p, item, false);
         if (!mbar_wait(bar_q_full, it & 1, abort_flag, p.timeout)) break;
         tc_fence_after();
-        for (int j = 0; j <= w.n && ok; j++) {
-            if (j < w.n) {  // S_j = Q K_j^T
+        // Issue S_js = Q K_js^T and O += P_jp V_jp in whichever order their inputs
+        // arrive (S first when both can go): a late K tile then no longer holds
+        // back a PV whose P and V are ready.  S_js reuses the TMEM buffer of
+        // P_{js-2}, so it waits until PV_{js-2} is issued (the MMAs run in issue
+        // order).  A phase seen complete cannot advance before it is consumed
+        // (its next arrival needs this issue first), so polling is exact.
+        int js = 0, jp = 0;
+        bool o_free = false;  // the previous item's epilogue has read O
+        long long t0 = 0;
+        bool waiting = false;
+        while (jp < w.n) {
+            bool issued = false;
+            if (js < w.n && jp >= js - 1) {
                 const int st = gk % C::KS;
-                if (!mbar_wait(&bar_k_full[st], (gk / C::KS) & 1, abort_flag, p.timeout)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_s = tmem + C::S_COL0 + ((g + j) & 1) * 64;
-                const uint64_t dk_st = dk0 + (uint64_t)((st * C::KV_BYTES) >> 4);
+                if (mbar_try_wait(&bar_k_full[st], (gk / C::KS) & 1)) {
+                    tc_fence_after();
+                    const uint32_t d_s = tmem + C::S_COL0 + ((g + js) & 1) * 64;
+                    const uint64_t dk_st = dk0 + (uint64_t)((st * C::KV_BYTES) >> 4);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++) {
-                    const uint64_t a = dq0 + (uint64_t)(((kk >> 2) * C::Q_SLAB + (kk & 3) * 32) >> 4);
-                    const uint64_t b = dk_st + (uint64_t)(((kk >> 2) * C::KV_SLAB + (kk & 3) * 32) >> 4);
-                    mma_ss(d_s, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        const uint64_t a = dq0 + (uint64_t)(((kk >> 2) * C::Q_SLAB + (kk & 3) * 32) >> 4);
+                        const uint64_t b = dk_st + (uint64_t)(((kk >> 2) * C::KV_SLAB + (kk & 3) * 32) >> 4);
+                        mma_ss(d_s, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
+                    }
+                    tc_commit(&bar_s_full[(g + js) & 1]);
+                    tc_commit(&bar_k_empty[st]);
+                    if (js == w.n - 1) tc_commit(bar_q_empty);
+                    gk++;
+                    js++;
+                    issued = true;
                 }
-                tc_commit(&bar_s_full[(g + j) & 1]);
-                tc_commit(&bar_k_empty[st]);
-                if (j == w.n - 1) tc_commit(bar_q_empty);
-                gk++;
             }
-            if (j >= 1) {  // O += P_{j-1} V_{j-1}
-                const int jj = j - 1;
-                const uint32_t gg = g + jj;
+            if (jp < js) {
+                const uint32_t gg = g + jp;
                 const int buf = gg & 1;
-                if (!mbar_wait(&bar_p_full[buf], (gg >> 1) & 1, abort_flag, p.timeout)) {
-                    ok = false;
-                    break;
-                }
-                if (jj == 0 && !mbar_wait(bar_o_empty, (it & 1) ^ 1, abort_flag, p.timeout)) {
-                    ok = false;
-                    break;
-                }
                 const int sv = gv % C::VS;
-                if (!mbar_wait(&bar_v_full[sv], (gv / C::VS) & 1, abort_flag, p.timeout)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t a_tmem = tmem + C::S_COL0 + buf * 64;  // P occupies the first 32 columns of S
+                if (jp == 0 && !o_free) o_free = mbar_try_wait(bar_o_empty, (it & 1) ^ 1);
+                if ((jp > 0 || o_free) && mbar_try_wait(&bar_p_full[buf], (gg >> 1) & 1) &&
+                    mbar_try_wait(&bar_v_full[sv], (gv / C::VS) & 1)) {
+                    tc_fence_after();
+                    const uint32_t a_tmem = tmem + C::S_COL0 + buf * 64;  // P occupies the first 32 columns of S
 #pragma unroll
-                for (int kk = 0; kk < 4; kk++) {
-                    const uint64_t b = dv0 + (uint64_t)((sv * C::KV_BYTES + kk * 2048) >> 4);
-                    mma_ts(tmem + C::O_COL, a_tmem + kk * 8, b, IDESC_PV, (jj > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint64_t b = dv0 + (uint64_t)((sv * C::KV_BYTES + kk * 2048) >> 4);
+                        mma_ts(tmem + C::O_COL, a_tmem + kk * 8, b, IDESC_PV, (jp > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&bar_v_empty[sv]);
+                    tc_commit(bar_o_done);
+                    gv++;
+                    jp++;
+                    issued = true;
                 }
-                tc_commit(&bar_v_empty[sv]);
-                tc_commit(bar_o_done);
-                gv++;
+            }
+            if (issued) {
+                waiting = false;
+            } else if (!waiting) {
+                t0 = clock64();
+                waiting = true;
+            } else if (*abort_flag || clock64() - t0 > p.timeout) {
+                *abort_flag = 1;
+                ok = false;
+                break;
             }
         }
+        if (!ok) break;
         g += w.n;
     }
     if (*abort_flag) {  // wait (bounded) for every MMA issued so far before TMEM is released
@@ -602,8 +640,8 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                 if (vec) {
                     uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
 #pragma unroll
-                    for (int i = 0; i < 4; i++)
-                        dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                    for (int i = 0; i < 4; i++)  // written once, read by the next layer: do not keep in L2 over K/V
+                        __stcs(dst + i, make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]));
                 } else {
                     uint16_t* dst = reinterpret_cast<uint16_t*>(orow + 32 * c);
 #pragma unroll
@@ -751,20 +789,27 @@ __device__ __noinline__ void peer_complete(const FwdParams& p) {
 template <int D, bool BF16, int MODE>
 __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ FwdParams p) {
     using C = Cfg<D>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // The 128-byte swizzle of the tiles assumes 1024-byte aligned tile bases; the
+    // region has no static shared memory before it, so this holds, and is checked.
+    if (smem_u32(smem_raw) & 1023) {
+        if (threadIdx.x == 0) atomicOr(&p.ws[2], HB_DEV_SMEM_ALIGN);
+        return;
+    }
+    uint8_t* sQ = smem_raw;
     uint8_t* sK = sQ + C::Q_BYTES;
     uint8_t* sV = sK + C::KS * C::KV_BYTES;
-
-    __shared__ __align__(8) uint64_t bar_q_full, bar_q_empty, bar_o_done, bar_o_empty, bar_drain;
-    __shared__ __align__(8) uint64_t bar_k_full[C::KS], bar_k_empty[C::KS], bar_v_full[C::VS], bar_v_empty[C::VS];
-    __shared__ __align__(8) uint64_t bar_s_full[2], bar_p_full[2], bar_item_full[2], bar_item_empty[2];
-    __shared__ int item_slot[2];
-    __shared__ uint32_t tmem_base_sh;
-    __shared__ int abort_sh;
-    __shared__ __align__(8) uint64_t bar_wg;
-    __shared__ int wg_flag;
+    typename C::Ctl* ctl = reinterpret_cast<typename C::Ctl*>(smem_raw + C::CTL_OFF);
+    uint64_t &bar_q_full = ctl->q_full, &bar_q_empty = ctl->q_empty, &bar_o_done = ctl->o_done;
+    uint64_t &bar_o_empty = ctl->o_empty, &bar_drain = ctl->drain, &bar_wg = ctl->wg;
+    uint64_t *bar_k_full = ctl->k_full, *bar_k_empty = ctl->k_empty;
+    uint64_t *bar_v_full = ctl->v_full, *bar_v_empty = ctl->v_empty;
+    uint64_t *bar_s_full = ctl->s_full, *bar_p_full = ctl->p_full;
+    uint64_t *bar_item_full = ctl->item_full, *bar_item_empty = ctl->item_empty;
+    int* item_slot = ctl->item_slot;
+    uint32_t& tmem_base_sh = ctl->tmem_base;
+    int& abort_sh = ctl->abort;
+    int& wg_flag = ctl->wg_flag;
     volatile int* abort_flag = &abort_sh;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

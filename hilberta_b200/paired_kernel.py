@@ -51,7 +51,7 @@ def device_status(device=None, *, clear=True) -> int:
             word = int(ws[2].item())
             bits |= word
             if clear:
-                (ws if word & _lib.HB_DEV_TIMEOUT else ws[2]).zero_()
+                (ws if word & (_lib.HB_DEV_TIMEOUT | _lib.HB_DEV_SMEM_ALIGN) else ws[2]).zero_()
     return bits
 
 

@@ -52,6 +52,7 @@ extern "C" {
 #define HB_DEV_BAD_COUNT 2     /* kv_counts entry outside [0, W]; clamped                */
 #define HB_DEV_BAD_BLOCK 4     /* kv_indices entry outside [0, N/64); its tile read zeros */
 #define HB_DEV_PEER_TIMEOUT 8  /* hb_paired_fwd_allgather: a peer's completion flag never came */
+#define HB_DEV_SMEM_ALIGN 16   /* shared memory not 1024-byte aligned: nothing computed      */
 
 /* Human-readable text for a status code (static storage). */
 const char* hb_status_string(int code);
