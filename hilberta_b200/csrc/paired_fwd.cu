@@ -437,7 +437,7 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
             bool issued = false;
             if (js < w.n && jp >= js - 1) {
                 const int st = gk % C::KS;
-                if (mbar_try_wait(&bar_k_full[st], (gk / C::KS) & 1)) {
+                if (mbar_test_wait(&bar_k_full[st], (gk / C::KS) & 1)) {
                     tc_fence_after();
                     const uint32_t d_s = tmem + C::S_COL0 + ((g + js) & 1) * 64;
                     const uint64_t dk_st = dk0 + (uint64_t)((st * C::KV_BYTES) >> 4);
@@ -459,9 +459,9 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
                 const uint32_t gg = g + jp;
                 const int buf = gg & 1;
                 const int sv = gv % C::VS;
-                if (jp == 0 && !o_free) o_free = mbar_try_wait(bar_o_empty, (it & 1) ^ 1);
-                if ((jp > 0 || o_free) && mbar_try_wait(&bar_p_full[buf], (gg >> 1) & 1) &&
-                    mbar_try_wait(&bar_v_full[sv], (gv / C::VS) & 1)) {
+                if (jp == 0 && !o_free) o_free = mbar_test_wait(bar_o_empty, (it & 1) ^ 1);
+                if ((jp > 0 || o_free) && mbar_test_wait(&bar_p_full[buf], (gg >> 1) & 1) &&
+                    mbar_test_wait(&bar_v_full[sv], (gv / C::VS) & 1)) {
                     tc_fence_after();
                     const uint32_t a_tmem = tmem + C::S_COL0 + buf * 64;  // P occupies the first 32 columns of S
 #pragma unroll
@@ -582,14 +582,19 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                 for (int i = 0; i < 32; i++) pk[i] = 0u;
             }
             tmem_st32(s_addr, pk);
-            // O may only be rescaled once PV_{gg-1} has completed; waiting on every
-            // entry also keeps this thread's o_done phase tracking exact.
-            if (j > 0) {
+            // O may only be rescaled once PV_{gg-1} has completed.  S_gg being ready
+            // means PV_{gg-2} completed (it was issued first), and PV_gg waits for
+            // this step's P, so o_done is at phase gg-1 or gg: waiting on the parity
+            // of gg-1 is exact without having waited the earlier phases.  Only a
+            // rescale needs that wait, and the item's last step, after which the
+            // epilogue waits on the last PV with the same two-phase guarantee.
+            const bool need = (m_new != m) && (m != -INFINITY);
+            const bool rescale = __any_sync(FULL, need);
+            if (j > 0 && (rescale || j == w.n - 1)) {
                 if (!warp_wait(bar_o_done, (gg - 1) & 1, abort_flag, p.timeout)) return;
                 tc_fence_after();
             }
-            const bool need = (m_new != m) && (m != -INFINITY);
-            if (__any_sync(FULL, need)) {
+            if (rescale) {
                 const float a = need ? alpha : 1.f;
 #pragma unroll
                 for (int c = 0; c < D / 32; c++) {
