@@ -486,57 +486,96 @@ def permutation_side_timing(a, q, k, v, metas, plan, dev, hb, steps=5):
 
 
 def run_e2e(a, q, k, v, metas, flops, world, dev, hb, fused=None):
-    """Same metric through the public call with HOST buffers: per call, pinned
-    Q/K/V host->device, the attention (at N > 1 this rank's heads fused with the
-    all-gather, PeerAllGather), and the output this rank consumes (all heads at
-    N > 1) device->host."""
+    """Same metric through the public call with HOST buffers, streamed the way a
+    caller feeding the attention from host memory would: call i's Q/K/V go
+    host->device (pinned) on a copy stream while call i-1 computes, and call
+    i-1's output goes device->host on another copy stream while call i
+    computes; device inputs and outputs are double-buffered and ordered by
+    events.  Every call's inputs cross PCIe in and its output crosses back out
+    inside the timed region.  At N > 1 the attention is this rank's heads fused
+    with the all-gather (PeerAllGather) and each rank reads back all heads."""
     import torch.distributed as dist
 
     hq, hk, hv = (x.detach().cpu().contiguous().pin_memory() for x in (q, k, v))
     B, hr, N, D = q.shape
-    hout = torch.empty((B, hr * world, N, D), dtype=q.dtype).pin_memory()
-    dq, dk, dv = (torch.empty_like(x, device=dev) for x in (hq, hk, hv))
-    dout = torch.empty_like(dq)
+    hout = [torch.empty((B, hr * world, N, D), dtype=q.dtype).pin_memory() for _ in range(2)]
+    dins = [[torch.empty_like(x, device=dev) for x in (hq, hk, hv)] for _ in range(2)]
+    douts = [torch.empty((B, hr, N, D), dtype=q.dtype, device=dev) for _ in range(2)]
     steps = max(1, min(a.steps, 5))
     kw = dict(global_strategy="triton", num_warps=8, num_stages=2)
+    compute = torch.cuda.current_stream(dev)
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event()
 
-    def one(ph):
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        if fused is None:
-            res = hb.paired_attention(dq, dk, dv, metas[ph], out=dout, **kw)
-        else:
-            res = fused(dq, dk, dv, metas[ph], **kw)
-        hout.copy_(res, non_blocking=True)
+    def run(n_calls):
+        loaded = [None, None]   # event: inputs of buffer b are on the device
+        consumed = [ev(), ev()]  # event: compute finished reading inputs of buffer b
+        written = [None, None]  # event: output buffer b holds a result to read back
+        drained = [ev(), ev()]  # event: output buffer b was copied to the host
+        for e in (*consumed, *drained):
+            e.record(compute)
+        pending = None
+        for i in range(n_calls + 1):
+            b = i & 1
+            if i < n_calls:  # stage call i's inputs
+                with torch.cuda.stream(h2d):
+                    h2d.wait_event(consumed[b])
+                    for dst, src in zip(dins[b], (hq, hk, hv)):
+                        dst.copy_(src, non_blocking=True)
+                    loaded[b] = ev()
+                    loaded[b].record(h2d)
+            if pending is not None:  # read back the previous call's output
+                pb, res = pending
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(written[pb])
+                    hout[pb].copy_(res, non_blocking=True)
+                    drained[pb].record(d2h)
+                pending = None
+            if i < n_calls:  # compute call i
+                ph = i % 4
+                compute.wait_event(loaded[b])
+                compute.wait_event(drained[b])
+                if fused is not None and i > 0:
+                    # peers write the buffer of call i-1 again during their call
+                    # i+1, which may start once this rank's call i has finished:
+                    # its read-back must be ordered before call i
+                    compute.wait_event(drained[b ^ 1])
+                if fused is None:
+                    res = hb.paired_attention(*dins[b], metas[ph], out=douts[b], **kw)
+                else:
+                    res = fused(*dins[b], metas[ph], **kw)
+                consumed[b].record(compute)
+                written[b] = ev()
+                written[b].record(compute)
+                pending = (b, res)
+        compute.wait_stream(h2d)
+        compute.wait_stream(d2h)
 
     with torch.inference_mode():
-        for ph in range(4):
-            one(ph)
+        run(4)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            for ph in range(4):
-                one(ph)
-        e1.record()
+        e0.record(compute)
+        run(4 * steps)
+        e1.record(compute)
         torch.cuda.synchronize()
     ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms[0])
-    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv)) * 4 * world
-    d2h = hout.numel() * hout.element_size() * 4 * world
+    h2d_bytes = sum(x.numel() * x.element_size() for x in (hq, hk, hv)) * 4 * world
+    d2h_bytes = hout[0].numel() * hout[0].element_size() * 4 * world
     return {
         "value": round(sum(flops) * steps / (ms * 1e-3) / 1e12, 3),
         "unit": "TFLOP/s",
         "ms_per_step": round(ms / steps, 3),
-        "h2d_bytes_per_step": h2d,
-        "d2h_bytes_per_step": d2h,
+        "h2d_bytes_per_step": h2d_bytes,
+        "d2h_bytes_per_step": d2h_bytes,
         "steps": steps,
-        "note": "per call: pinned Q/K/V H2D + attention + O D2H through the public API"
+        "note": "per call: pinned Q/K/V H2D + attention + O D2H through the public API, copies of neighbouring calls "
+        "overlapped on two copy streams"
         + (" (head_parallel.PeerAllGather: local heads in, all heads out)" if fused is not None else " (paired_attention)"),
     }
 
