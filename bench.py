@@ -591,7 +591,7 @@ def cpu_baseline(a, plan, active, bounded=15.0):
     H = a.heads
     N, G = plan.total_tokens, plan.global_tokens
     p = plan.phases[0]
-    bm = ao.block_mask_from_rows(p.kv_indices.numpy(), p.kv_counts.numpy(), N, G)
+    bm = ao.block_mask_from_rows(np.asarray(p.kv_indices), np.asarray(p.kv_counts), N, G)
     row_active = bm.sum(1).repeat(64)  # active key blocks per query row
     g = torch.Generator().manual_seed(2707)
     q, k, v = (torch.randn(1, H, N, 128, generator=g).to(torch.bfloat16) for _ in range(3))
@@ -638,7 +638,7 @@ def run_reference(a):
     N, G = plan.total_tokens, plan.global_tokens
     active = [(G // 64) * (N // 64) + int(p.kv_counts.sum()) for p in plan.phases]
     steps = max(1, a.steps)
-    per_step = max(2.0, 60.0 / (steps + max(3, a.warmup)))
+    per_step = min(a.cpu_seconds, max(2.0, 60.0 / (steps + max(3, a.warmup))))
     vals = []
     cpu = None
     for i in range(max(1, min(a.warmup, 1)) + steps):
