@@ -8,17 +8,23 @@
 // 71-75; ALL_QUERIES mode).
 //
 // B200 design (one CTA = 8 warps, two CTAs per SM, persistent):
-//   warp 0  item fetcher (atomic work counter, LPT order) + TMA loads of Q, K
-//   warp 1  TMA loads of V
+//   warp 0  item fetcher (atomic work counter; global-row chunks first, then
+//           ordinary pair-rows head-major) + TMA loads of Q and K (3 stages)
+//   warp 1  TMA loads of V (2 stages)
 //   warp 2  single-thread tcgen05.mma issuer: S = Q K^T (SS, 128x64x16 steps)
-//           into TMEM, O += P V (TS: P read from TMEM, V MN-major from SMEM)
+//           into TMEM, O += P V (TS: P read from TMEM, V MN-major from SMEM),
+//           each issued as soon as its inputs are ready (non-blocking polls)
 //   warp 3  TMEM allocator
 //   warps 4-7  softmax: one TMEM lane (query row) per thread, exp2 online
 //           softmax with lazy O rescaling (only when the running max grows by
 //           more than 2^8), P written back into the S columns as 16-bit pairs,
-//           epilogue O / l -> global memory.
+//           epilogue O / l -> the output (or this rank's rows to every rank's
+//           output, fused all-gather), or a chunk's partial for split rows.
 // TMEM per CTA: S0 [0,64) S1 [64,128) O [128,128+D) (256 columns; two CTAs fill
-// the 512-column TMEM of an SM).  Tiles use the 128-byte swizzle end to end.
+// the 512-column TMEM of an SM).  Tiles use the 128-byte swizzle end to end;
+// mbarriers live after the tiles in the (1024-byte aligned) dynamic region.
+// Token layouts (template MODE): physical order (tiled maps), any permutation
+// (row map, tile::gather4), raster order by 8x8 image squares (5-D maps).
 // Every mbarrier wait is bounded; a timeout sets HB_DEV_TIMEOUT and the CTA
 // drains and exits instead of hanging.  No cluster multicast anywhere.
 #include <cuda.h>
