@@ -120,7 +120,9 @@ struct Cfg {
         uint64_t q_full, q_empty, o_done, o_empty, drain, wg;
         uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
         uint64_t s_full[2], p_full[2], item_full[2], item_empty[2];
+        uint64_t push_full[2], push_empty[2];  // fused all-gather: finished items handed to warp 3
         int item_slot[2];
+        int push_item[2];
         uint32_t tmem_base;
         int abort;
         int wg_flag;
@@ -503,12 +505,74 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
     }
 }
 
+// Fused all-gather, run by warp 3 while the softmax warps go on with the next
+// item: each finished item's 128 output rows, already in this rank's output, are
+// read back from L2 and stored to every other rank with lane-consecutive 16-byte
+// stores (whole rows per instruction).  Items arrive through a two-slot ring;
+// item -1 ends the loop.
+template <int D, bool BF16>
+__device__ void pusher(const FwdParams& p, uint64_t* bar_full, uint64_t* bar_empty, const int* push_item,
+                       volatile int* abort_flag) {
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    constexpr int CPR = D / 8;          // 16-byte chunks per row
+    constexpr int RPI = 32 / CPR;       // rows per warp instruction
+    constexpr int NI = 128 / RPI;       // instructions per destination for the item's 128 rows
+    constexpr int BATCH = NI < 8 ? NI : 8;
+    const int lane = threadIdx.x & 31;
+    const T* src = reinterpret_cast<const T*>(p.outs[p.rank]);
+    for (uint32_t k = 0;; k++) {
+        const int ps = k & 1;
+        if (!warp_wait(&bar_full[ps], (k >> 1) & 1, abort_flag, p.timeout)) return;
+        const int item = push_item[ps];
+        if (item < 0) return;
+        const Item w = decode_item(p, item, false);
+        const int64_t hb_off = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh;
+        const int row0 = w.qrow0 + lane / CPR;
+        // loads in batches ahead of their stores: the destinations could alias the
+        // source as far as the compiler knows
+#pragma unroll 1
+        for (int i0 = 0; i0 < NI; i0 += BATCH) {
+            uint4 v4[BATCH];
+#pragma unroll
+            for (int i = 0; i < BATCH; i++)
+                v4[i] = __ldcg(reinterpret_cast<const uint4*>(src + hb_off + (int64_t)(row0 + (i0 + i) * RPI) * p.o_sn) +
+                               lane % CPR);
+            for (int d = 0; d < p.n_out; d++) {
+                if (d == p.rank) continue;
+                T* dst = reinterpret_cast<T*>(p.outs[d]) + hb_off;
+#pragma unroll
+                for (int i = 0; i < BATCH; i++)
+                    *(reinterpret_cast<uint4*>(dst + (int64_t)(row0 + (i0 + i) * RPI) * p.o_sn) + lane % CPR) = v4[i];
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_empty[ps]);
+    }
+}
+
+// Softmax warps' side of the ring: the warp's rows are in the output (fenced to
+// GPU scope, so warp 3 reads them back from L2), then the item (or -1 to end)
+// goes into the next slot once warp 3 has emptied it.
+__device__ __forceinline__ bool enqueue_push(const FwdParams& p, uint64_t* bar_full, uint64_t* bar_empty,
+                                             int* push_item, uint32_t& npush, int item, volatile int* abort_flag) {
+    const int ps = npush & 1;
+    if (!warp_wait(&bar_empty[ps], ((npush >> 1) & 1) ^ 1, abort_flag, p.timeout)) return false;
+    __threadfence();
+    if (threadIdx.x == 128) push_item[ps] = item;
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&bar_full[ps]);
+    npush++;
+    return true;
+}
+
 template <int D, bool BF16, int MODE>
 __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_item_full, uint64_t* bar_item_empty,
                              int* item_slot, uint64_t* bar_s_full, uint64_t* bar_p_full, uint64_t* bar_o_done,
-                             uint64_t* bar_o_empty, uint64_t* bar_wg, int* wg_flag, volatile int* abort_flag) {
+                             uint64_t* bar_o_empty, uint64_t* bar_wg, int* wg_flag, uint64_t* bar_push_full,
+                             uint64_t* bar_push_empty, int* push_item, volatile int* abort_flag) {
     using C = Cfg<D>;
     const int r = threadIdx.x - 128;  // query row within the tile == TMEM lane
+    uint32_t npush = 0;               // items handed to the pusher (fused all-gather)
     uint32_t wg_uses = 0;             // phases of bar_wg (the 4 softmax warps) used so far
     const int lane = threadIdx.x & 31;
     const int half = r >> 6;
@@ -521,7 +585,10 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
         const int item = item_slot[slot];
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_item_empty[slot]);
-        if (item >= p.num_items) return;
+        if (item >= p.num_items) {
+            if (p.n_out > 1) enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, -1, abort_flag);
+            return;
+        }
         const Item w = decode_item(p, item, false);
         float m = -INFINITY, l = 0.f;
         int chunk = 0;
@@ -636,10 +703,9 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
         const int64_t ooff = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh + (int64_t)(row_ok ? orow : 0) * p.o_sn;
         // every destination has the same address residue mod 16 (checked on the host)
         const bool vec = (reinterpret_cast<uintptr_t>(reinterpret_cast<T*>(p.outs[0]) + ooff) & 15) == 0;
-        // Rows are written to this rank's output first (lane = row); with vector
-        // alignment, push_rows then copies the warp's finished rows to the other
-        // ranks with lane-consecutive 16-byte stores (whole rows per instruction,
-        // the shape that keeps NVLink writes full), re-reading them from L2.
+        // Rows are written to this rank's output first (lane = row); in the fused
+        // all-gather the item is then handed to warp 3 (pusher), which copies the
+        // rows to the other ranks while this warp goes on with the next item.
         const bool push = p.n_out > 1 && vec;
         auto store_row = [&](int c, const float* vals) {  // 32 output columns from 32 fp32 values
             uint32_t packed[16];
@@ -663,33 +729,6 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                 }
             }
         };
-        auto push_rows = [&]() {  // the warp's 32 rows, already in outs[rank], to every other rank
-            constexpr int CPR = D / 8;     // 16-byte chunks per row
-            constexpr int RPI = 32 / CPR;  // rows per warp instruction
-            __syncwarp();                  // the lanes' row stores are visible to the whole warp
-            const int row0 = w.qrow0 + (r & ~31) + lane / CPR;
-            const int64_t hb_off = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh;
-            const T* src = reinterpret_cast<const T*>(p.outs[p.rank]);
-            // loads in batches of 8 ahead of their stores: the destinations could
-            // alias the source as far as the compiler knows, so interleaving
-            // would serialise every load behind the previous store
-            constexpr int NI = 32 / RPI, BATCH = NI < 8 ? NI : 8;
-#pragma unroll
-            for (int i0 = 0; i0 < NI; i0 += BATCH) {
-                uint4 v4[BATCH];
-#pragma unroll
-                for (int i = 0; i < BATCH; i++)
-                    v4[i] = __ldcg(reinterpret_cast<const uint4*>(src + hb_off + (int64_t)(row0 + (i0 + i) * RPI) * p.o_sn) +
-                                   lane % CPR);
-                for (int d = 0; d < p.n_out; d++) {
-                    if (d == p.rank) continue;
-                    T* dst = reinterpret_cast<T*>(p.outs[d]) + hb_off;
-#pragma unroll
-                    for (int i = 0; i < BATCH; i++)
-                        *(reinterpret_cast<uint4*>(dst + (int64_t)(row0 + (i0 + i) * RPI) * p.o_sn) + lane % CPR) = v4[i];
-                }
-            }
-        };
         if (!w.split) {
             const float inv = 1.f / l;
 #pragma unroll
@@ -704,7 +743,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_o_empty);
-            if (push) push_rows();
+            if (push && !enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, item, abort_flag)) return;
         } else {
             constexpr int PSTRIDE = 128 * D + 256;
             float* rec = p.partial + ((int64_t)w.group * p.n_chunks + w.chunk) * PSTRIDE;
@@ -771,7 +810,8 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                     for (int i = 0; i < 32; i++) vals[i] *= inv;
                     store_row(c, vals);
                 }
-                if (push) push_rows();
+                if (push && !enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, item, abort_flag))
+                    return;
             }
         }
         g += w.n;
@@ -844,6 +884,8 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
             mbar_init(&bar_p_full[i], 4);
             mbar_init(&bar_item_full[i], 1);
             mbar_init(&bar_item_empty[i], 6);  // V producer, MMA issuer, 4 softmax warps
+            mbar_init(&ctl->push_full[i], 4);
+            mbar_init(&ctl->push_empty[i], 1);
         }
         abort_sh = 0;
         fence_barrier_init();
@@ -875,7 +917,10 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
                                 &bar_o_done, &bar_o_empty, &bar_drain, abort_flag);
     } else if (warp >= 4) {
         softmax_role<D, BF16, MODE>(p, tmem, bar_item_full, bar_item_empty, item_slot, bar_s_full, bar_p_full, &bar_o_done,
-                              &bar_o_empty, &bar_wg, &wg_flag, abort_flag);
+                              &bar_o_empty, &bar_wg, &wg_flag, ctl->push_full, ctl->push_empty, ctl->push_item,
+                              abort_flag);
+    } else if (warp == 3 && p.n_out > 1) {
+        pusher<D, BF16>(p, ctl->push_full, ctl->push_empty, ctl->push_item, abort_flag);
     }
     tc_fence_before();
     __syncthreads();
@@ -1134,9 +1179,9 @@ int paired_fwd(const void* q, const void* k, const void* v, void* out, const int
         for (int i = 0; i < n; i++) {
             if (!peers->out[i] || !peers->flags[i] || (reinterpret_cast<uintptr_t>(peers->flags[i]) & 3))
                 return HB_ERR_ARG;
-            if (((reinterpret_cast<uintptr_t>(peers->out[i]) ^ reinterpret_cast<uintptr_t>(peers->out[0])) & 15))
-                return HB_ERR_ARG;  // one vector-store decision serves every destination
+            if (reinterpret_cast<uintptr_t>(peers->out[i]) & 15) return HB_ERR_ARG;  // 16-byte row stores
         }
+        if (strides[9] % 8 || strides[10] % 8 || strides[11] % 8) return HB_ERR_ARG;
     }
     if (row_map && (reinterpret_cast<uintptr_t>(row_map) & 15)) return HB_ERR_ARG;
     if (workspace_bytes < hb_fwd_workspace_bytes() || (reinterpret_cast<uintptr_t>(workspace) & 255))
