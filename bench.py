@@ -242,6 +242,16 @@ def run_native(a):
     total_ms = t0.elapsed_time(t1)
     per_phase = [[ev[s][ph][0].elapsed_time(ev[s][ph][1]) for s in range(a.steps)] for ph in range(4)]
     kern_ms = [statistics.mean(x) for x in per_phase]
+
+    def pct(xs, q):  # nearest-rank percentile of one phase's per-call times
+        ys = sorted(xs)
+        return ys[min(len(ys) - 1, max(0, math.ceil(q * len(ys)) - 1))]
+
+    phase_stats = {
+        "median": [round(statistics.median(x), 4) for x in per_phase],
+        "p10": [round(pct(x, 0.10), 4) for x in per_phase],
+        "p90": [round(pct(x, 0.90), 4) for x in per_phase],
+    }
     t = torch.tensor([total_ms, *kern_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -280,6 +290,7 @@ def run_native(a):
         "ms_per_step": round(total_ms / a.steps, 4),
         "ms_per_call": round(weighted_ms, 4),
         "ms_per_call_by_phase": [round(x, 4) for x in kern_ms],
+        "ms_per_call_by_phase_stats": phase_stats,  # this rank's per-call distribution (rank 0)
         "eff_tflops_kernel": round(weighted_flop / (weighted_ms * 1e-3) / 1e12, 2),
         "frac_peak": round(achieved / peak, 4),
         "higher_is_better": True,
