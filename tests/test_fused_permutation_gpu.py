@@ -141,3 +141,14 @@ def test_raster_squares_bad_origin_drops_block():
     dropped = rows[good.text_tokens + 3 * 64 : good.text_tokens + 4 * 64]
     assert bool((out[:, :, dropped] == 7.0).all())  # the bad block's rows were never written
     assert bool(torch.isfinite(out).all())
+
+
+@pytest.mark.parametrize("mode", ["squares", "rows"])
+def test_raster_orders_with_split_global_rows(mode):
+    """Both raster-order layouts while the global rows are split over chunks
+    (8 heads at 1024^2), bit-identical to the explicit reorder."""
+    if mode == "squares":
+        fused, ref, _ = _raster_case(16, 3, 64, 8, "bhnd", 2, 64)
+    else:
+        fused, ref, _ = _case(16, 3, 64, 8, "bhnd", 2, 65)
+    assert torch.equal(fused, ref)

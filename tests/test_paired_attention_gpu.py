@@ -225,3 +225,47 @@ def test_shared_workspace_across_split_shapes():
     _run(q[:, :2], k[:, :2], v[:, :2], meta64)  # few groups: partials right after the counters
     assert torch.equal(_run(q, k, v, meta64), fresh)
     assert torch.equal(_run(q, k, v, meta64), fresh)
+
+
+def _unsplit(q, k, v, meta):
+    """The same call through the C ABI with the minimal workspace (global rows run unsplit)."""
+    import ctypes
+
+    from hilberta_b200 import _lib
+    from hilberta_b200.paired_kernel import LOG2E
+
+    out = torch.empty_like(q)
+    ws = torch.zeros(64, dtype=torch.int32, device=q.device)  # 256 bytes: no room for split partials
+    B, H, N, D = q.shape
+    strides = (ctypes.c_int64 * 12)(*q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *out.stride()[:3])
+    rc = _lib.lib().hb_paired_fwd(
+        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), strides, B, H, N, D, meta.global_tokens,
+        int(meta.kv_indices.shape[1]), 64, _lib.ptr(meta.kv_indices), _lib.ptr(meta.kv_flags),
+        _lib.ptr(meta.kv_counts), float(D**-0.5 * LOG2E), 1 if q.dtype == torch.bfloat16 else 0, None,
+        _lib.ptr(ws), 256, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(ws[2].item()) == 0
+    return out
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.float16, 64), (torch.bfloat16, 64), (torch.float16, 128)])
+def test_split_global_rows_fp16_and_d64(dtype, D):
+    """Global rows split over key-block chunks (8 heads at 1024^2: 3 chunks per row)
+    for fp16 and D=64, against the oracle and against the unsplit launch."""
+    import hilberta_b200 as hb
+
+    plan = hb.bridge_k_plan(16, 3, False, grid_size=64)
+    meta, p = _meta(plan, 2)
+    N, G = plan.total_tokens, plan.global_tokens
+    q, k, v = (x.cuda() for x in ao.seeded_qkv(1, 8, N, D, seed=31, dtype=dtype))
+    out = _run(q, k, v, meta)
+    rows = np.concatenate([np.arange(0, G), np.arange(G, N, 11)])
+    ref = ao.masked_attention_fp32(q.cpu(), k.cpu(), v.cpu(), ao.block_mask_from_rows(p.kv_indices, p.kv_counts, N, G),
+                                   rows=rows)
+    _close(out[:, :, torch.from_numpy(rows).cuda()], ref, f"split {dtype} D{D}")
+    with torch.inference_mode():
+        whole = _unsplit(q, k, v, meta)
+    _close(whole[:, :, torch.from_numpy(rows).cuda()], ref, "unsplit")
+    assert torch.equal(out[:, :, G:], whole[:, :, G:])  # ordinary rows take the same path either way
+    assert not torch.equal(out[:, :, :G], whole[:, :, :G])  # the global rows really were merged from chunks
