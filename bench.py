@@ -635,7 +635,6 @@ def run_reference(a):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    import hilberta_b200  # noqa: F401  (plan built on the GPU when one is present)
 
     res, tiles, k = CONFIGS[a.config]
     if torch.cuda.is_available():

@@ -23,7 +23,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .paired_kernel import LOG2E, _check_inputs, _launch_allgather, paired_attention  # noqa: F401
+from .paired_kernel import _check_inputs, _launch_allgather, paired_attention
 
 
 def head_range(num_heads: int, rank: int, world: int) -> tuple[int, int]:
