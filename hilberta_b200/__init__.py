@@ -4,12 +4,21 @@ Drop-in for the reference's operator API (``hilberta``): plan builders
 (``build_plan``, ``bridge_k_plan``), metadata (``pair_metadata``,
 ``validate_metadata``) and the paired block-sparse attention
 (``paired_attention``), all executed by the sm_100a library in ``lib/``.
+
+Additions beyond that API: raster-order tensors (``raster_order``,
+``token_order_map`` for ``paired_attention(token_order=...)``), the adapter's
+plan cache (``PlanBank``), the processor's Q/K/V preparation
+(``prepare_qkv``), and head-parallel attention over several GPUs with the head
+all-gather fused into the kernel (``PeerAllGather``).
 """
 
 from .bridge_k import bridge_k_plan
-from .paired_kernel import device_status, paired_attention
+from .head_parallel import PeerAllGather, all_gather_heads, head_parallel_attention
+from .paired_kernel import RasterOrder, device_status, paired_attention, raster_order, token_order_map
 from .paired_metadata import PairedMetadata, pair_metadata, unpair_metadata
 from .plan import AttentionPlan, PhasePlan, build_plan, full_attention_plan
+from .plan_bank import PlanBank
+from .prep import norm_rope_pack, prepare_qkv
 from .sparse_kernel import explicit_mask, validate_metadata
 
 __version__ = "0.1.0"
@@ -27,4 +36,13 @@ __all__ = [
     "explicit_mask",
     "paired_attention",
     "device_status",
+    "RasterOrder",
+    "raster_order",
+    "token_order_map",
+    "PlanBank",
+    "prepare_qkv",
+    "norm_rope_pack",
+    "PeerAllGather",
+    "all_gather_heads",
+    "head_parallel_attention",
 ]
