@@ -9,7 +9,8 @@ Additions beyond that API: raster-order tensors (``raster_order``,
 ``token_order_map`` for ``paired_attention(token_order=...)``), the adapter's
 plan cache (``PlanBank``), the processor's Q/K/V preparation
 (``prepare_qkv``), and head-parallel attention over several GPUs with the head
-all-gather fused into the kernel (``PeerAllGather``).
+all-gather fused into the kernel (``PeerAllGather``), and the FLUX processor
+built from them (``HilbertAProcessor``).
 """
 
 from .bridge_k import bridge_k_plan
@@ -19,6 +20,7 @@ from .paired_metadata import PairedMetadata, pair_metadata, unpair_metadata
 from .plan import AttentionPlan, PhasePlan, build_plan, full_attention_plan
 from .plan_bank import PlanBank
 from .prep import norm_rope_pack, prepare_qkv
+from .processor import HilbertAProcessor
 from .sparse_kernel import explicit_mask, validate_metadata
 
 __version__ = "0.1.0"
@@ -45,4 +47,5 @@ __all__ = [
     "PeerAllGather",
     "all_gather_heads",
     "head_parallel_attention",
+    "HilbertAProcessor",
 ]
