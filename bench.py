@@ -17,6 +17,12 @@ all ranks over NVLink peer memory (head_parallel.PeerAllGather).  ``value`` =
 total active FLOP of all ranks / max-over-ranks device time.  The kernel
 followed by an NCCL all-gather is timed beside it (``nccl_path``).
 
+At N = 1 the line also carries ``flux_step``: one denoising step of a
+FLUX.1-architecture transformer with random weights (19 + 38 blocks, hidden
+3072, 11.9 B parameters) at this config, with HilbertA attention in every
+joint-attention call, next to the same step with dense attention
+(``--no-flux-step`` skips it).
+
 ``--impl reference`` times the reference's dense-mask CPU path (plan mask +
 fp32 SDPA, the computation of hilberta/flux_adapter.py:299-307) restated in
 oracle/attention_oracle.py, on a bounded row sample, with all host threads.
@@ -65,6 +71,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU seconds of the baseline sample")
+    ap.add_argument("--no-flux-step", action="store_true",
+                    help="skip the FLUX.1-architecture denoising step (random weights), HilbertA vs dense attention")
     return ap.parse_args()
 
 
@@ -263,6 +271,9 @@ def run_native(a):
 
     perm = permutation_side_timing(a, q, k, v, metas, plan, dev, hb) if world == 1 else None
     prep_t = prep_side_timing(plan, H, dev) if world == 1 else None
+    flux = None
+    if world == 1 and not a.no_flux_step:
+        flux = flux_step_timing(a, dev, weighted_ms * 57)
     nccl = nccl_side_timing(a, q, k, v, metas, flops, world, dev, hb) if world > 1 else None
 
     e2e = None
@@ -342,6 +353,8 @@ def run_native(a):
             "frac": round(max(t_tensor, t_link) * 1e3 / weighted_ms, 4),
         }
         line["nccl_path"] = nccl
+    if flux is not None:
+        line["flux_step"] = flux
     if e2e is not None:
         line["e2e"] = e2e
     if clk.result is not None:
@@ -404,6 +417,67 @@ def prep_side_timing(plan, H, dev, steps=10, D=128):
     res["bytes"] = nbytes
     res["achieved_gbs"] = round(nbytes / (res["ms"] * 1e-3) / 1e9, 1)
     res["note"] = "Q,K,V: per-head RMSNorm + text/image cat + rotary + [B,S,H,D] pack (hb_norm_rope_pack) vs eager torch"
+    return res
+
+
+def flux_step_timing(a, dev, paired_ms_per_step, steps=3, warmup=2):
+    """One denoising step of a FLUX.1-architecture transformer with random
+    weights (19 double + 38 single blocks, hidden 3072, 24 x 128 heads, 512 text
+    tokens; hilberta_b200/flux_model.py) at this config's resolution, with
+    HilbertA attention (the plan's 16-tile K3 phases, layer i on phase i % 4) in
+    every joint-attention call, against the same weights with dense attention.
+    Inputs are device-resident; the step includes the entry/exit permutation."""
+    from hilberta_b200 import PlanBank, bridge_k_plan
+    from hilberta_b200.flux_model import FluxLikeTransformer, parameter_count
+
+    res_px, tiles, k = CONFIGS[a.config]
+    grid = res_px // 16
+    plan = bridge_k_plan(tiles, k, False, grid_size=grid)
+    bank = PlanBank(plan)
+    torch.manual_seed(5)
+    model = FluxLikeTransformer(grid, bank, attention="hilberta", device=dev)
+    g = torch.Generator(device="cpu").manual_seed(6)
+    latents = torch.randn(1, grid * grid, 64, generator=g).to(torch.bfloat16).to(dev)
+    text = torch.randn(1, plan.text_tokens, 4096, generator=g).to(torch.bfloat16).to(dev)
+    pooled = torch.randn(1, 768, generator=g).to(torch.bfloat16).to(dev)
+    t, guid = torch.tensor([0.75], device=dev), torch.tensor([3.5], device=dev)
+    res = {"workload": f"FLUX.1-architecture step, {a.config}, 19+38 blocks, hidden 3072, random weights",
+           "parameters": parameter_count(model)}
+    outs = {}
+    with torch.inference_mode():
+        for mode in ("hilberta", "dense"):
+            model.set_attention(mode)
+            for _ in range(warmup):
+                model(latents, text, pooled, t, guid)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                out = model(latents, text, pooled, t, guid)
+            e1.record()
+            torch.cuda.synchronize()
+            res[f"{mode}_ms"] = round(e0.elapsed_time(e1) / steps, 2)
+            outs[mode] = out.float()
+        # one dense attention call on the step's shapes, for the attention share
+        N = plan.total_tokens
+        q = torch.randn(1, 24, N, 128, device=dev, dtype=torch.bfloat16)
+        for _ in range(3):
+            torch.nn.functional.scaled_dot_product_attention(q, q, q)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(5):
+            torch.nn.functional.scaled_dot_product_attention(q, q, q)
+        e1.record()
+        torch.cuda.synchronize()
+    dense_call = e0.elapsed_time(e1) / 5
+    res["speedup"] = round(res["dense_ms"] / res["hilberta_ms"], 3)
+    res["attention_ms_hilberta"] = round(paired_ms_per_step, 2)  # 57 calls at the phase-weighted kernel time
+    res["attention_ms_dense"] = round(57 * dense_call, 2)  # 57 torch SDPA calls, same shapes
+    res["rel_diff_vs_dense"] = round(float((outs["hilberta"] - outs["dense"]).norm() / outs["dense"].norm()), 4)
+    res["note"] = ("steps=%d warmup=%d, device-resident inputs; rel_diff_vs_dense is the sparse step's relative "
+                   "L2 distance from the dense step (a property of the sparse pattern, not an error)" % (steps, warmup))
+    del model
+    torch.cuda.empty_cache()
     return res
 
 

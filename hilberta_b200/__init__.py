@@ -10,7 +10,9 @@ Additions beyond that API: raster-order tensors (``raster_order``,
 plan cache (``PlanBank``), the processor's Q/K/V preparation
 (``prepare_qkv``), and head-parallel attention over several GPUs with the head
 all-gather fused into the kernel (``PeerAllGather``), and the FLUX processor
-built from them (``HilbertAProcessor``).
+built from them (``HilbertAProcessor``), and a FLUX.1-architecture transformer
+with random weights that runs a denoising step on it (``FluxLikeTransformer``,
+imported from ``hilberta_b200.flux_model``).
 """
 
 from .bridge_k import bridge_k_plan

@@ -1,0 +1,269 @@
+"""A FLUX.1-architecture transformer with random weights, for timing one
+denoising step with HilbertA attention in every joint-attention call.
+
+The architecture follows FLUX.1's published design (the model the reference
+adapts, hilberta/flux_adapter.py): 19 double-stream blocks (separate weights
+for text and image tokens, one joint attention), 38 single-stream blocks
+(attention and MLP in parallel on the joined sequence), hidden 3072, 24 heads of
+128, per-head RMSNorm on Q/K, 3-axis rotary embedding (16/56/56 dimensions over
+(index, row, column) positions), adaLN-Zero modulation from the timestep
+embedding, tanh-GELU MLPs with ratio 4.  Weights are random (no checkpoint is
+available); the step's cost and data flow are the model's.
+
+Attention runs through ``HilbertAProcessor`` (fused Q/K/V preparation + paired
+block-sparse attention on the layer's phase) or, for the comparison, the same
+prepared Q/K/V through dense scaled-dot-product attention.  Image tokens are
+permuted into the plan's physical order once per step at entry and back at exit
+(the reference's sampling layout, hilberta/sampling_layout.py:88-116).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .prep import norm_rope_pack
+from .processor import HilbertAProcessor
+
+
+class RMSNormWeight(torch.nn.Module):
+    """The per-head RMSNorm parameters the processors read (``weight``, ``eps``)."""
+
+    def __init__(self, d, dtype, device):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.ones(d, dtype=dtype, device=device), requires_grad=False)
+        self.eps = 1e-6
+
+
+def _linear(i, o, dtype, device, std=0.02):
+    lin = torch.nn.Linear(i, o, dtype=dtype, device=device)
+    with torch.no_grad():
+        lin.weight.normal_(0.0, std)
+        lin.bias.zero_()
+    return lin.requires_grad_(False)
+
+
+class JointAttention(torch.nn.Module):
+    """Attribute layout of a FLUX attention module; ``processor`` does the work."""
+
+    def __init__(self, dim, heads, head_dim, double, dtype, device):
+        super().__init__()
+        inner = heads * head_dim
+        self.heads = heads
+        self.to_q, self.to_k, self.to_v = (_linear(dim, inner, dtype, device) for _ in range(3))
+        self.norm_q, self.norm_k = RMSNormWeight(head_dim, dtype, device), RMSNormWeight(head_dim, dtype, device)
+        self.added_kv_proj_dim = dim if double else None
+        if double:
+            self.add_q_proj, self.add_k_proj, self.add_v_proj = (_linear(dim, inner, dtype, device) for _ in range(3))
+            self.norm_added_q = RMSNormWeight(head_dim, dtype, device)
+            self.norm_added_k = RMSNormWeight(head_dim, dtype, device)
+            self.to_out = torch.nn.ModuleList([_linear(inner, dim, dtype, device), torch.nn.Dropout(0.0)])
+            self.to_add_out = _linear(inner, dim, dtype, device)
+        self.processor = None
+
+    def forward(self, hidden_states, encoder_hidden_states=None, image_rotary_emb=None):
+        return self.processor(self, hidden_states, encoder_hidden_states, image_rotary_emb=image_rotary_emb)
+
+
+class DenseProcessor:
+    """The same steps as ``HilbertAProcessor`` with dense attention over all
+    tokens, or over the plan's dense mask of the layer's phase when ``bank`` is
+    given (the correctness reference of the sparse step)."""
+
+    def __init__(self, bank=None, layer=0):
+        self.bank, self.phase = bank, int(layer) % 4
+
+    def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, image_rotary_emb=None):
+        if attention_mask is not None:
+            raise ValueError("External attention masks are not supported")
+        cos, sin = image_rotary_emb
+        h = attn.heads
+        if encoder_hidden_states is not None:
+            q = norm_rope_pack(attn.add_q_proj(encoder_hidden_states), attn.to_q(hidden_states), heads=h,
+                               weight_txt=attn.norm_added_q.weight, weight_img=attn.norm_q.weight, cos=cos, sin=sin)
+            k = norm_rope_pack(attn.add_k_proj(encoder_hidden_states), attn.to_k(hidden_states), heads=h,
+                               weight_txt=attn.norm_added_k.weight, weight_img=attn.norm_k.weight, cos=cos, sin=sin)
+            v = norm_rope_pack(attn.add_v_proj(encoder_hidden_states), attn.to_v(hidden_states), heads=h)
+        else:
+            q = norm_rope_pack(None, attn.to_q(hidden_states), heads=h, weight_txt=attn.norm_q.weight,
+                               weight_img=attn.norm_q.weight, cos=cos, sin=sin)
+            k = norm_rope_pack(None, attn.to_k(hidden_states), heads=h, weight_txt=attn.norm_k.weight,
+                               weight_img=attn.norm_k.weight, cos=cos, sin=sin)
+            v = norm_rope_pack(None, attn.to_v(hidden_states), heads=h)
+        mask = None if self.bank is None else self.bank.dense_mask(self.phase, q.device)
+        out = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), attn_mask=mask)
+        out = out.transpose(1, 2).flatten(2, 3).to(hidden_states.dtype)
+        if encoder_hidden_states is None:
+            return out
+        text, image = out.split_with_sizes([encoder_hidden_states.shape[1], out.shape[1] - encoder_hidden_states.shape[1]], 1)
+        return attn.to_out[1](attn.to_out[0](image)), attn.to_add_out(text)
+
+
+def _modulate(x, shift, scale):
+    return F.layer_norm(x, x.shape[-1:], eps=1e-6) * (1 + scale[:, None]) + shift[:, None]
+
+
+class DoubleStreamBlock(torch.nn.Module):
+    def __init__(self, dim, heads, head_dim, dtype, device):
+        super().__init__()
+        self.mod_img = _linear(dim, 6 * dim, dtype, device)
+        self.mod_txt = _linear(dim, 6 * dim, dtype, device)
+        self.attn = JointAttention(dim, heads, head_dim, True, dtype, device)
+        self.ff_img = torch.nn.ModuleList([_linear(dim, 4 * dim, dtype, device), _linear(4 * dim, dim, dtype, device)])
+        self.ff_txt = torch.nn.ModuleList([_linear(dim, 4 * dim, dtype, device), _linear(4 * dim, dim, dtype, device)])
+
+    def forward(self, img, txt, temb, rot):
+        mi = self.mod_img(F.silu(temb)).chunk(6, dim=-1)
+        mt = self.mod_txt(F.silu(temb)).chunk(6, dim=-1)
+        a_img, a_txt = self.attn(_modulate(img, mi[0], mi[1]), _modulate(txt, mt[0], mt[1]), rot)
+        img = img + mi[2][:, None] * a_img
+        txt = txt + mt[2][:, None] * a_txt
+        img = img + mi[5][:, None] * self.ff_img[1](F.gelu(self.ff_img[0](_modulate(img, mi[3], mi[4])), approximate="tanh"))
+        txt = txt + mt[5][:, None] * self.ff_txt[1](F.gelu(self.ff_txt[0](_modulate(txt, mt[3], mt[4])), approximate="tanh"))
+        return img, txt
+
+
+class SingleStreamBlock(torch.nn.Module):
+    def __init__(self, dim, heads, head_dim, dtype, device):
+        super().__init__()
+        self.mod = _linear(dim, 3 * dim, dtype, device)
+        self.attn = JointAttention(dim, heads, head_dim, False, dtype, device)
+        self.proj_mlp = _linear(dim, 4 * dim, dtype, device)
+        self.proj_out = _linear(dim + 4 * dim, dim, dtype, device)
+
+    def forward(self, x, temb, rot):
+        shift, scale, gate = self.mod(F.silu(temb)).chunk(3, dim=-1)
+        h = _modulate(x, shift, scale)
+        mlp = F.gelu(self.proj_mlp(h), approximate="tanh")
+        a = self.attn(h, None, rot).to(x.dtype)
+        return x + gate[:, None] * self.proj_out(torch.cat([a, mlp], dim=-1))
+
+
+def timestep_features(t, dim=256, max_period=10000.0):
+    """Sinusoidal features [B, dim] of scalar times ``t`` [B] (scaled by 1000,
+    cosines first, as FLUX's time embedding takes them)."""
+    half = dim // 2
+    freqs = torch.exp(-torch.log(torch.tensor(max_period, dtype=torch.float32, device=t.device))
+                      * torch.arange(half, dtype=torch.float32, device=t.device) / half)
+    ang = (t.float() * 1000.0)[:, None] * freqs[None]
+    return torch.cat([torch.cos(ang), torch.sin(ang)], dim=1)
+
+
+class ConditioningEmbedder(torch.nn.Module):
+    """temb = MLP(time features) + MLP(guidance features) + MLP(pooled text)."""
+
+    def __init__(self, dim, pooled_dim, dtype, device):
+        super().__init__()
+        mlp = lambda i: torch.nn.ModuleList([_linear(i, dim, dtype, device), _linear(dim, dim, dtype, device)])
+        self.time, self.guidance, self.text = mlp(256), mlp(256), mlp(pooled_dim)
+
+    def forward(self, timestep, guidance, pooled):
+        run = lambda m, x: m[1](F.silu(m[0](x)))
+        dt = pooled.dtype
+        temb = run(self.time, timestep_features(timestep).to(dt)) + run(self.text, pooled)
+        if guidance is not None:
+            temb = temb + run(self.guidance, timestep_features(guidance).to(dt))
+        return temb
+
+
+def rotary_3axis(ids, axes=(16, 56, 56), theta=10000.0):
+    """cos/sin [N, sum(axes)] fp32 of 3-axis positions ``ids`` [N, 3]: per axis,
+    frequencies theta^(-2i/d) on that coordinate, each repeated for its pair."""
+    cos, sin = [], []
+    for a, d in enumerate(axes):
+        freqs = 1.0 / theta ** (torch.arange(0, d, 2, dtype=torch.float64, device=ids.device) / d)
+        ang = ids[:, a].to(torch.float64)[:, None] * freqs[None]
+        cos.append(torch.cos(ang).repeat_interleave(2, dim=1))
+        sin.append(torch.sin(ang).repeat_interleave(2, dim=1))
+    return torch.cat(cos, 1).float().contiguous(), torch.cat(sin, 1).float().contiguous()
+
+
+class FluxLikeTransformer(torch.nn.Module):
+    """``forward(latents [B, n, 64], text [B, T, text_dim], pooled [B, 768],
+    timestep [B], guidance [B] or None)`` -> ``[B, n, 64]`` for a ``grid x grid``
+    image in raster order.
+
+    ``attention``: "hilberta" (``HilbertAProcessor`` on ``bank``), "dense" (all
+    tokens), or "masked" (dense attention under ``bank``'s phase masks).  With a
+    bank, image tokens run in the plan's physical order whatever the attention;
+    ``set_attention`` switches processors on the same weights."""
+
+    def __init__(self, grid, bank=None, attention="hilberta", num_double=19, num_single=38, dim=3072, heads=24,
+                 head_dim=128, in_channels=64, text_dim=4096, pooled_dim=768, text_tokens=512, dtype=torch.bfloat16, device="cuda",
+                 kernel_options=None):
+        super().__init__()
+        self.grid, self.bank = grid, bank
+        self.x_embedder = _linear(in_channels, dim, dtype, device)
+        self.context_embedder = _linear(text_dim, dim, dtype, device)
+        self.cond = ConditioningEmbedder(dim, pooled_dim, dtype, device)
+        self.double_blocks = torch.nn.ModuleList(DoubleStreamBlock(dim, heads, head_dim, dtype, device) for _ in range(num_double))
+        self.single_blocks = torch.nn.ModuleList(SingleStreamBlock(dim, heads, head_dim, dtype, device) for _ in range(num_single))
+        self.mod_out = _linear(dim, 2 * dim, dtype, device)
+        self.proj_out = _linear(dim, in_channels, dtype, device)
+        self.kernel_options = kernel_options
+        self.set_attention(attention)
+        # positions: text (0, 0, 0); image (0, row, col), in the token order the step uses
+        g = grid
+        rows = torch.arange(g * g, device=device) // g
+        cols = torch.arange(g * g, device=device) % g
+        img_ids = torch.stack([torch.zeros_like(rows), rows, cols], dim=1)
+        self.order = self.inverse = None
+        if bank is not None:
+            if bank.image_tokens != g * g:
+                raise ValueError("The plan's image-token count does not match the grid")
+            entry = bank.on_device(torch.device(device))
+            self.order, self.inverse = entry["order"], entry["inverse"]
+            img_ids = img_ids.index_select(0, self.order)
+        self.text_tokens = bank.text_tokens if bank is not None else text_tokens
+        ids = torch.cat([torch.zeros(self.text_tokens, 3, dtype=img_ids.dtype, device=device), img_ids])
+        self.rot = rotary_3axis(ids)
+
+    def set_attention(self, attention):
+        if attention not in ("hilberta", "dense", "masked"):
+            raise ValueError("attention must be 'hilberta', 'dense' or 'masked'")
+        if attention != "dense" and self.bank is None:
+            raise ValueError(f"attention={attention!r} needs a PlanBank")
+        attn_modules = [b.attn for b in self.double_blocks] + [b.attn for b in self.single_blocks]
+        for layer, m in enumerate(attn_modules):
+            if attention == "hilberta":
+                m.processor = HilbertAProcessor(self.bank, layer, self.kernel_options)
+            else:
+                m.processor = DenseProcessor(self.bank if attention == "masked" else None, layer)
+        self.attention = attention
+
+    def forward(self, latents, text, pooled, timestep, guidance=None):
+        if latents.shape[1] != self.grid * self.grid or text.shape[1] != self.text_tokens:
+            raise ValueError("latent or text token count does not match the model")
+        if self.order is not None:  # into the plan's physical order, once per step
+            latents = latents.index_select(1, self.order)
+        temb = self.cond(timestep, guidance, pooled)
+        img = self.x_embedder(latents)
+        txt = self.context_embedder(text)
+        for b in self.double_blocks:
+            img, txt = b(img, txt, temb, self.rot)
+        x = torch.cat([txt, img], dim=1)
+        for b in self.single_blocks:
+            x = b(x, temb, self.rot)
+        img = x[:, txt.shape[1]:]
+        shift, scale = self.mod_out(F.silu(temb)).chunk(2, dim=-1)
+        out = self.proj_out(_modulate(img, shift, scale))
+        if self.order is not None:
+            out = out.index_select(1, self.inverse)
+        return out
+
+
+def parameter_count(model) -> int:
+    return sum(p.numel() for p in model.parameters())
+
+
+def attention_flops_per_step(bank, heads=24, head_dim=128, layers=57):
+    """Active-block FLOPs of the step's attention calls (phase of layer i = i % 4)."""
+    total = 0
+    for layer in range(layers):
+        p = bank.phases[layer % 4]
+        active = (bank.global_tokens // 64) * (bank.total_tokens // 64) + int(p[1].sum())
+        total += heads * 4 * 64 * 64 * head_dim * active
+    return total
+
+
+__all__ = ["FluxLikeTransformer", "DenseProcessor", "ConditioningEmbedder", "timestep_features", "rotary_3axis", "parameter_count", "attention_flops_per_step"]
