@@ -17,11 +17,11 @@ all ranks over NVLink peer memory (head_parallel.PeerAllGather).  ``value`` =
 total active FLOP of all ranks / max-over-ranks device time.  The kernel
 followed by an NCCL all-gather is timed beside it (``nccl_path``).
 
-At N = 1 the line also carries ``flux_step``: one denoising step of a
+The line also carries ``flux_step``: one denoising step of a
 FLUX.1-architecture transformer with random weights (19 + 38 blocks, hidden
 3072, 11.9 B parameters) at this config, with HilbertA attention in every
-joint-attention call, next to the same step with dense attention
-(``--no-flux-step`` skips it).
+joint-attention call, next to the same step with dense attention; at N > 1
+tensor-parallel over the ranks (``--no-flux-step`` skips it).
 
 ``--impl reference`` times the reference's dense-mask CPU path (plan mask +
 fp32 SDPA, the computation of hilberta/flux_adapter.py:299-307) restated in
@@ -271,9 +271,7 @@ def run_native(a):
 
     perm = permutation_side_timing(a, q, k, v, metas, plan, dev, hb) if world == 1 else None
     prep_t = prep_side_timing(plan, H, dev) if world == 1 else None
-    flux = None
-    if world == 1 and not a.no_flux_step:
-        flux = flux_step_timing(a, dev, weighted_ms * 57)
+    flux = None if a.no_flux_step else flux_step_timing(a, dev, world)
     nccl = nccl_side_timing(a, q, k, v, metas, flops, world, dev, hb) if world > 1 else None
 
     e2e = None
@@ -420,63 +418,79 @@ def prep_side_timing(plan, H, dev, steps=10, D=128):
     return res
 
 
-def flux_step_timing(a, dev, paired_ms_per_step, steps=3, warmup=2):
+def flux_step_timing(a, dev, world, steps=3, warmup=2):
     """One denoising step of a FLUX.1-architecture transformer with random
     weights (19 double + 38 single blocks, hidden 3072, 24 x 128 heads, 512 text
     tokens; hilberta_b200/flux_model.py) at this config's resolution, with
-    HilbertA attention (the plan's 16-tile K3 phases, layer i on phase i % 4) in
-    every joint-attention call, against the same weights with dense attention.
-    Inputs are device-resident; the step includes the entry/exit permutation."""
-    from hilberta_b200 import PlanBank, bridge_k_plan
+    HilbertA attention (the plan's phases, layer i on phase i % 4) in every
+    joint-attention call, against the same weights with dense attention.
+    N > 1: tensor-parallel over the ranks (hilberta_b200/flux_tp.py), each rank
+    attending over its 24/N heads; times are the max over ranks.  Inputs are
+    device-resident; the step includes the entry/exit permutation.  The
+    attention parts are timed alone: 57 paired calls (phases cycled) and 57
+    dense SDPA calls on this rank's heads."""
+    import torch.distributed as dist
+
+    from hilberta_b200 import PlanBank, bridge_k_plan, paired_attention
     from hilberta_b200.flux_model import FluxLikeTransformer, parameter_count
 
     res_px, tiles, k = CONFIGS[a.config]
     grid = res_px // 16
     plan = bridge_k_plan(tiles, k, False, grid_size=grid)
     bank = PlanBank(plan)
-    torch.manual_seed(5)
+    torch.manual_seed(5)  # identical weights on every rank
     model = FluxLikeTransformer(grid, bank, attention="hilberta", device=dev)
+    params = parameter_count(model)
+    if world > 1:
+        from hilberta_b200.flux_tp import shard_flux_model
+
+        shard_flux_model(model)
     g = torch.Generator(device="cpu").manual_seed(6)
     latents = torch.randn(1, grid * grid, 64, generator=g).to(torch.bfloat16).to(dev)
     text = torch.randn(1, plan.text_tokens, 4096, generator=g).to(torch.bfloat16).to(dev)
     pooled = torch.randn(1, 768, generator=g).to(torch.bfloat16).to(dev)
     t, guid = torch.tensor([0.75], device=dev), torch.tensor([3.5], device=dev)
-    res = {"workload": f"FLUX.1-architecture step, {a.config}, 19+38 blocks, hidden 3072, random weights",
-           "parameters": parameter_count(model)}
-    outs = {}
+    N, hr = plan.total_tokens, 24 // world
+    qkv = [torch.randn(1, hr, N, 128, device=dev, dtype=torch.bfloat16) for _ in range(3)]
+    metas = bank.on_device(dev)["paired_phases"]
+
+    def timed(fn, n):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    times, outs = {}, {}
     with torch.inference_mode():
         for mode in ("hilberta", "dense"):
             model.set_attention(mode)
-            for _ in range(warmup):
-                model(latents, text, pooled, t, guid)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(steps):
-                out = model(latents, text, pooled, t, guid)
-            e1.record()
-            torch.cuda.synchronize()
-            res[f"{mode}_ms"] = round(e0.elapsed_time(e1) / steps, 2)
-            outs[mode] = out.float()
-        # one dense attention call on the step's shapes, for the attention share
-        N = plan.total_tokens
-        q = torch.randn(1, 24, N, 128, device=dev, dtype=torch.bfloat16)
-        for _ in range(3):
-            torch.nn.functional.scaled_dot_product_attention(q, q, q)
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(5):
-            torch.nn.functional.scaled_dot_product_attention(q, q, q)
-        e1.record()
-        torch.cuda.synchronize()
-    dense_call = e0.elapsed_time(e1) / 5
+            times[f"{mode}_ms"] = timed(lambda: model(latents, text, pooled, t, guid), steps)
+            outs[mode] = model(latents, text, pooled, t, guid).float()
+        times["attention_ms_hilberta"] = timed(lambda: [paired_attention(*qkv, metas[i % 4]) for i in range(57)], 1)
+        times["attention_ms_dense"] = timed(
+            lambda: [torch.nn.functional.scaled_dot_product_attention(*qkv) for _ in range(57)], 1)
+    vals = torch.tensor(list(times.values()), dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    res = {"workload": f"FLUX.1-architecture step, {a.config}, 19+38 blocks, hidden 3072, random weights",
+           "parameters": params,
+           "parallelism": f"tensor-parallel x{world} (heads and MLP hidden sharded, NCCL all-reduce)"
+           if world > 1 else "single GPU"}
+    res.update({key: round(float(x), 2) for key, x in zip(times, vals)})
     res["speedup"] = round(res["dense_ms"] / res["hilberta_ms"], 3)
-    res["attention_ms_hilberta"] = round(paired_ms_per_step, 2)  # 57 calls at the phase-weighted kernel time
-    res["attention_ms_dense"] = round(57 * dense_call, 2)  # 57 torch SDPA calls, same shapes
     res["rel_diff_vs_dense"] = round(float((outs["hilberta"] - outs["dense"]).norm() / outs["dense"].norm()), 4)
-    res["note"] = ("steps=%d warmup=%d, device-resident inputs; rel_diff_vs_dense is the sparse step's relative "
-                   "L2 distance from the dense step (a property of the sparse pattern, not an error)" % (steps, warmup))
-    del model
+    res["note"] = ("steps=%d warmup=%d, device-resident inputs, max over ranks; attention_ms_* = 57 calls on this "
+                   "rank's heads; rel_diff_vs_dense is the sparse step's relative L2 distance from the dense step "
+                   "(a property of the sparse pattern, not an error)" % (steps, warmup))
+    del model, outs, qkv
     torch.cuda.empty_cache()
     return res
 

@@ -10,7 +10,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 OUT = PKG / "lib" / "libhilberta_b200.so"
-SOURCES = ("builder.cu", "paired_fwd.cu", "peer.cu", "prep.cu")
+SOURCES = ("builder.cu", "paired_fwd.cu", "peer.cu", "prep.cu", "block_ops.cu")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

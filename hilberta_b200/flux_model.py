@@ -22,6 +22,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
+from .block_ops import NativeBlockOps
 from .prep import norm_rope_pack
 from .processor import HilbertAProcessor
 
@@ -100,7 +101,22 @@ class DenseProcessor:
 
 
 def _modulate(x, shift, scale):
+    """adaLN of the output layer (once per step, eager)."""
     return F.layer_norm(x, x.shape[-1:], eps=1e-6) * (1 + scale[:, None]) + shift[:, None]
+
+
+class JoinedLinear(torch.nn.Module):
+    """FLUX's single-stream ``proj_out`` over [attention | MLP hidden]: one
+    weight ``[dim, inner + hidden]``, applied as ``ops.joined_linear`` so the
+    concatenated input is never materialised."""
+
+    def __init__(self, inner, hidden, dim, dtype, device):
+        super().__init__()
+        full = _linear(inner + hidden, dim, dtype, device)
+        self.weight, self.bias, self.split = full.weight, full.bias, inner
+
+    def forward(self, a, m, ops):
+        return ops.joined_linear(a, m, self.weight[:, : self.split], self.weight[:, self.split :], self.bias)
 
 
 class DoubleStreamBlock(torch.nn.Module):
@@ -112,15 +128,15 @@ class DoubleStreamBlock(torch.nn.Module):
         self.ff_img = torch.nn.ModuleList([_linear(dim, 4 * dim, dtype, device), _linear(4 * dim, dim, dtype, device)])
         self.ff_txt = torch.nn.ModuleList([_linear(dim, 4 * dim, dtype, device), _linear(4 * dim, dim, dtype, device)])
 
-    def forward(self, img, txt, temb, rot):
+    def forward(self, img, txt, temb, rot, ops):
         mi = self.mod_img(F.silu(temb)).chunk(6, dim=-1)
         mt = self.mod_txt(F.silu(temb)).chunk(6, dim=-1)
-        a_img, a_txt = self.attn(_modulate(img, mi[0], mi[1]), _modulate(txt, mt[0], mt[1]), rot)
-        img = img + mi[2][:, None] * a_img
-        txt = txt + mt[2][:, None] * a_txt
-        img = img + mi[5][:, None] * self.ff_img[1](F.gelu(self.ff_img[0](_modulate(img, mi[3], mi[4])), approximate="tanh"))
-        txt = txt + mt[5][:, None] * self.ff_txt[1](F.gelu(self.ff_txt[0](_modulate(txt, mt[3], mt[4])), approximate="tanh"))
-        return img, txt
+        a_img, a_txt = self.attn(ops.modulate(img, mi[0], mi[1]), ops.modulate(txt, mt[0], mt[1]), rot)
+        img, h_img = ops.gate_add_modulate(img, a_img, mi[2], mi[3], mi[4])
+        txt, h_txt = ops.gate_add_modulate(txt, a_txt, mt[2], mt[3], mt[4])
+        f_img = self.ff_img[1](ops.linear_gelu(h_img, self.ff_img[0].weight, self.ff_img[0].bias))
+        f_txt = self.ff_txt[1](ops.linear_gelu(h_txt, self.ff_txt[0].weight, self.ff_txt[0].bias))
+        return ops.gate_add(img, f_img, mi[5]), ops.gate_add(txt, f_txt, mt[5])
 
 
 class SingleStreamBlock(torch.nn.Module):
@@ -129,14 +145,14 @@ class SingleStreamBlock(torch.nn.Module):
         self.mod = _linear(dim, 3 * dim, dtype, device)
         self.attn = JointAttention(dim, heads, head_dim, False, dtype, device)
         self.proj_mlp = _linear(dim, 4 * dim, dtype, device)
-        self.proj_out = _linear(dim + 4 * dim, dim, dtype, device)
+        self.proj_out = JoinedLinear(heads * head_dim, 4 * dim, dim, dtype, device)
 
-    def forward(self, x, temb, rot):
+    def forward(self, x, temb, rot, ops):
         shift, scale, gate = self.mod(F.silu(temb)).chunk(3, dim=-1)
-        h = _modulate(x, shift, scale)
-        mlp = F.gelu(self.proj_mlp(h), approximate="tanh")
-        a = self.attn(h, None, rot).to(x.dtype)
-        return x + gate[:, None] * self.proj_out(torch.cat([a, mlp], dim=-1))
+        h = ops.modulate(x, shift, scale)
+        mlp = ops.linear_gelu(h, self.proj_mlp.weight, self.proj_mlp.bias)
+        a = self.attn(h, None, rot)
+        return ops.gate_add(x, self.proj_out(a, mlp, ops), gate)
 
 
 def timestep_features(t, dim=256, max_period=10000.0):
@@ -186,12 +202,15 @@ class FluxLikeTransformer(torch.nn.Module):
     ``attention``: "hilberta" (``HilbertAProcessor`` on ``bank``), "dense" (all
     tokens), or "masked" (dense attention under ``bank``'s phase masks).  With a
     bank, image tokens run in the plan's physical order whatever the attention;
-    ``set_attention`` switches processors on the same weights."""
+    ``set_attention`` switches processors on the same weights.  ``block_ops``
+    (default ``NativeBlockOps``: the library's adaLN kernels and cuBLASLt
+    epilogues) runs the blocks' modulation, residual and MLP steps."""
 
     def __init__(self, grid, bank=None, attention="hilberta", num_double=19, num_single=38, dim=3072, heads=24,
                  head_dim=128, in_channels=64, text_dim=4096, pooled_dim=768, text_tokens=512, dtype=torch.bfloat16, device="cuda",
-                 kernel_options=None):
+                 kernel_options=None, block_ops=None):
         super().__init__()
+        self.ops = NativeBlockOps() if block_ops is None else block_ops
         self.grid, self.bank = grid, bank
         self.x_embedder = _linear(in_channels, dim, dtype, device)
         self.context_embedder = _linear(text_dim, dim, dtype, device)
@@ -240,10 +259,10 @@ class FluxLikeTransformer(torch.nn.Module):
         img = self.x_embedder(latents)
         txt = self.context_embedder(text)
         for b in self.double_blocks:
-            img, txt = b(img, txt, temb, self.rot)
+            img, txt = b(img, txt, temb, self.rot, self.ops)
         x = torch.cat([txt, img], dim=1)
         for b in self.single_blocks:
-            x = b(x, temb, self.rot)
+            x = b(x, temb, self.rot, self.ops)
         img = x[:, txt.shape[1]:]
         shift, scale = self.mod_out(F.silu(temb)).chunk(2, dim=-1)
         out = self.proj_out(_modulate(img, shift, scale))
@@ -266,4 +285,4 @@ def attention_flops_per_step(bank, heads=24, head_dim=128, layers=57):
     return total
 
 
-__all__ = ["FluxLikeTransformer", "DenseProcessor", "ConditioningEmbedder", "timestep_features", "rotary_3axis", "parameter_count", "attention_flops_per_step"]
+__all__ = ["FluxLikeTransformer", "DenseProcessor", "JoinedLinear", "ConditioningEmbedder", "timestep_features", "rotary_3axis", "parameter_count", "attention_flops_per_step"]

@@ -265,6 +265,24 @@ int hb_norm_rope_pack(const void* txt, int64_t txt_sb, int64_t txt_sn, const voi
                       const float* sin, const int32_t* image_rows, void* out, int64_t o_sb,
                       int64_t o_sn, int64_t o_sh, int dtype, int32_t* status, void* stream);
 
+/* ---- adaLN modulation and gated residual of the FLUX blocks -------------- */
+/* No counterpart in the reference's own code: the adaLN-Zero steps of the
+ * diffusers FLUX blocks that call the attention processor
+ * (hilberta/flux_adapter.py:259-340 wraps that processor), fused:
+ *   x' = x + gate[b] * y                              (when y is given)
+ *   h  = LayerNorm(x') * (1 + scale[b]) + shift[b]    (when h_out is given)
+ * over `rows` rows of C elements, row r in batch b = r / rows_per_batch.
+ * x, y, x_out, h_out: 16-bit (dtype 0 fp16, 1 bf16) rows with element row
+ * strides x_rs, y_rs, xo_rs, h_rs (x_out may alias x); gate/shift/scale: [B][C]
+ * with batch stride mod_bs, unit element stride.  LayerNorm without affine
+ * weights, eps as given; fp32 arithmetic, x' rounded to 16 bits before the
+ * LayerNorm, h rounded once.  C a multiple of 256 up to 4096; pointers 16-byte
+ * aligned, strides multiples of 8 elements. */
+int hb_adaln_residual(const void* x, int64_t x_rs, const void* y, int64_t y_rs, const void* gate,
+                      const void* shift, const void* scale, int64_t mod_bs, void* x_out,
+                      int64_t xo_rs, void* h_out, int64_t h_rs, int rows, int rows_per_batch, int C,
+                      float eps, int dtype, void* stream);
+
 /* ---- allocation-free variant of hb_paired_fwd --------------------------- */
 /* No counterpart in the reference: an addition for callers that must not
  * allocate device memory.  Some hosts cannot call cudaMalloc from the thread

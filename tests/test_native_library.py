@@ -152,3 +152,30 @@ def test_norm_rope_pack_argument_checks(lib):
     assert call(dtype=2) == _lib.HB_ERR_UNSUPPORTED
     assert call(img=ctypes.c_void_p((1 << 20) + 8)) == _lib.HB_ERR_ALIGN
     assert call(sn=260) == _lib.HB_ERR_ALIGN  # row stride not a multiple of 8 elements
+
+
+def test_adaln_residual_argument_checks(lib):
+    """hb_adaln_residual validates its optional-argument pairs, C and alignment
+    on the host; rows == 0 returns before any launch."""
+    from hilberta_b200 import _lib
+
+    f = ctypes.c_void_p(1 << 20)
+
+    def call(x=f, y=f, gate=f, shift=f, scale=f, x_out=f, h_out=f, rows=64, C=3072, rs=3072, mod_bs=18432,
+             eps=1e-6, dtype=1):
+        return lib.hb_adaln_residual(x, rs, y, rs, gate, shift, scale, mod_bs, x_out, rs, h_out, rs, rows, 64, C,
+                                     eps, dtype, None)
+
+    assert call(x=None) == _lib.HB_ERR_ARG
+    assert call(y=None, h_out=None) == _lib.HB_ERR_ARG  # nothing to compute
+    assert call(gate=None) == _lib.HB_ERR_ARG  # residual without its gate
+    assert call(x_out=None) == _lib.HB_ERR_ARG
+    assert call(shift=None) == _lib.HB_ERR_ARG  # modulation without shift
+    assert call(eps=-1.0) == _lib.HB_ERR_ARG
+    assert call(C=128) == _lib.HB_ERR_UNSUPPORTED  # not a multiple of 256
+    assert call(C=8192) == _lib.HB_ERR_UNSUPPORTED  # above 4096
+    assert call(dtype=3) == _lib.HB_ERR_UNSUPPORTED
+    assert call(y=ctypes.c_void_p((1 << 20) + 8)) == _lib.HB_ERR_ALIGN
+    assert call(rs=3076) == _lib.HB_ERR_ALIGN
+    assert call(rows=0) == _lib.HB_OK
+    assert call(y=None, gate=None, x_out=None, rows=0) == _lib.HB_OK  # modulation only
