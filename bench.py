@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU seconds of the baseline sample")
+    ap.add_argument("--tp-chunks", type=int, default=1,
+                    help="FLUX step at N > 1: row chunks of each row-parallel GEMM (all-reduce overlap)")
+    ap.add_argument("--tp-carveout", type=int, default=0, help="SMs kept free of those GEMMs for the all-reduce")
     ap.add_argument("--no-flux-step", action="store_true",
                     help="skip the FLUX.1-architecture denoising step (random weights), HilbertA vs dense attention")
     return ap.parse_args()
@@ -444,7 +447,7 @@ def flux_step_timing(a, dev, world, steps=3, warmup=2):
     if world > 1:
         from hilberta_b200.flux_tp import shard_flux_model
 
-        shard_flux_model(model)
+        shard_flux_model(model, chunks=a.tp_chunks, carveout=a.tp_carveout or None)
     g = torch.Generator(device="cpu").manual_seed(6)
     latents = torch.randn(1, grid * grid, 64, generator=g).to(torch.bfloat16).to(dev)
     text = torch.randn(1, plan.text_tokens, 4096, generator=g).to(torch.bfloat16).to(dev)
@@ -482,7 +485,8 @@ def flux_step_timing(a, dev, world, steps=3, warmup=2):
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     res = {"workload": f"FLUX.1-architecture step, {a.config}, 19+38 blocks, hidden 3072, random weights",
            "parameters": params,
-           "parallelism": f"tensor-parallel x{world} (heads and MLP hidden sharded, NCCL all-reduce)"
+           "parallelism": f"tensor-parallel x{world} (heads and MLP hidden sharded, NCCL all-reduce; "
+           f"{a.tp_chunks} row chunks per row-parallel GEMM, {a.tp_carveout} SMs carved out)"
            if world > 1 else "single GPU"}
     res.update({key: round(float(x), 2) for key, x in zip(times, vals)})
     res["speedup"] = round(res["dense_ms"] / res["hilberta_ms"], 3)

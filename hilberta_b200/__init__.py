@@ -7,7 +7,8 @@ Drop-in for the reference's operator API (``hilberta``): plan builders
 
 Additions beyond that API: raster-order tensors (``raster_order``,
 ``token_order_map`` for ``paired_attention(token_order=...)``), the adapter's
-plan cache (``PlanBank``), the processor's Q/K/V preparation
+plan cache (``PlanBank``), plans on disk (``save_plan``, ``load_plan``,
+``PlanCache``), the processor's Q/K/V preparation
 (``prepare_qkv``), and head-parallel attention over several GPUs with the head
 all-gather fused into the kernel (``PeerAllGather``), and the FLUX processor
 built from them (``HilbertAProcessor``), and a FLUX.1-architecture transformer
@@ -21,6 +22,7 @@ from .paired_kernel import RasterOrder, device_status, paired_attention, raster_
 from .paired_metadata import PairedMetadata, pair_metadata, unpair_metadata
 from .plan import AttentionPlan, PhasePlan, build_plan, full_attention_plan
 from .plan_bank import PlanBank
+from .plan_cache import PlanCache, load_plan, save_plan
 from .prep import norm_rope_pack, prepare_qkv
 from .processor import HilbertAProcessor
 from .sparse_kernel import explicit_mask, validate_metadata
@@ -44,6 +46,9 @@ __all__ = [
     "raster_order",
     "token_order_map",
     "PlanBank",
+    "PlanCache",
+    "save_plan",
+    "load_plan",
     "prepare_qkv",
     "norm_rope_pack",
     "PeerAllGather",

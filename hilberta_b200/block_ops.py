@@ -15,7 +15,6 @@ modulation output are fine).  LayerNorm without affine weights.
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 
@@ -121,12 +120,19 @@ class NativeBlockOps:
         return y.view(*x.shape[:-1], weight.shape[0])
 
     @staticmethod
-    def joined_linear(a, m, weight_a, weight_m, bias):
-        """[a | m] @ [weight_a | weight_m]^T + bias without materialising [a | m]."""
+    def joined_linear(a, m, weight_a, weight_m, bias, out=None):
+        """[a | m] @ [weight_a | weight_m]^T (+ bias) without materialising
+        [a | m]: two GEMMs, the second accumulating into the first's output
+        (``out``, rows x out-features, if given)."""
         a2, m2 = a.reshape(-1, a.shape[-1]), m.reshape(-1, m.shape[-1])
-        y = F.linear(a2, weight_a, bias)
-        y = torch.addmm(y, m2, weight_m.t(), out=y)
-        return y.view(*a.shape[:-1], weight_a.shape[0])
+        if out is None:
+            out = torch.empty(a2.shape[0], weight_a.shape[0], dtype=a.dtype, device=a.device)
+        if bias is None:
+            torch.mm(a2, weight_a.t(), out=out)
+        else:
+            torch.addmm(bias, a2, weight_a.t(), out=out)
+        out.addmm_(m2, weight_m.t())
+        return out.view(*a.shape[:-1], weight_a.shape[0])
 
 
 __all__ = ["adaln", "gate_residual", "gate_residual_adaln", "NativeBlockOps"]

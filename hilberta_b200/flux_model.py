@@ -286,3 +286,55 @@ def attention_flops_per_step(bank, heads=24, head_dim=128, layers=57):
 
 
 __all__ = ["FluxLikeTransformer", "DenseProcessor", "JoinedLinear", "ConditioningEmbedder", "timestep_features", "rotary_3axis", "parameter_count", "attention_flops_per_step"]
+
+
+def _main(argv=None):
+    """``python -m hilberta_b200.flux_model [--grid 128] [--tiles 16] [--k 3]
+    [--steps 3] [--profile]``: time one step with HilbertA and dense attention on
+    cuda:0 and, with ``--profile``, print the per-kernel device times of one
+    HilbertA step (torch.profiler)."""
+    import argparse
+
+    from . import PlanBank, bridge_k_plan
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--grid", type=int, default=128)
+    ap.add_argument("--tiles", type=int, default=16)
+    ap.add_argument("--k", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--profile", action="store_true")
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    plan = bridge_k_plan(a.tiles, a.k, False, grid_size=a.grid)
+    torch.manual_seed(5)
+    model = FluxLikeTransformer(a.grid, PlanBank(plan), attention="hilberta", device=dev)
+    g = torch.Generator().manual_seed(6)
+    x = (torch.randn(1, a.grid * a.grid, 64, generator=g).to(torch.bfloat16).to(dev),
+         torch.randn(1, plan.text_tokens, 4096, generator=g).to(torch.bfloat16).to(dev),
+         torch.randn(1, 768, generator=g).to(torch.bfloat16).to(dev),
+         torch.tensor([0.75], device=dev), torch.tensor([3.5], device=dev))
+    with torch.inference_mode():
+        for mode in ("hilberta", "dense"):
+            model.set_attention(mode)
+            for _ in range(2):
+                model(*x)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.steps):
+                model(*x)
+            e1.record()
+            torch.cuda.synchronize()
+            print(f"{mode}: {e0.elapsed_time(e1) / a.steps:.2f} ms/step")
+        if a.profile:
+            from torch.profiler import ProfilerActivity, profile
+
+            model.set_attention("hilberta")
+            with profile(activities=[ProfilerActivity.CUDA]) as p:
+                model(*x)
+                torch.cuda.synchronize()
+            print(p.key_averages().table(sort_by="cuda_time_total", row_limit=20, max_name_column_width=70))
+
+
+if __name__ == "__main__":
+    _main()

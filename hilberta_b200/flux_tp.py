@@ -25,11 +25,48 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
 
 
 def _param(t):
     return torch.nn.Parameter(t.detach().contiguous(), requires_grad=False)
+
+
+class _Overlap:
+    """Row-chunked GEMM + all-reduce: chunk i's all-reduce (async, on NCCL's
+    stream) runs while chunk i+1's GEMM computes.  cuBLAS GEMMs of this size
+    occupy every SM, so while the chunks are enqueued the matmuls are told to
+    leave ``carveout`` SMs free for the collective (torch's SM carve-out for
+    cuBLASLt); the previous setting is restored afterwards."""
+
+    def __init__(self, chunks, carveout, min_rows=2048):
+        self.chunks, self.carveout, self.min_rows = int(chunks), carveout, int(min_rows)
+
+    def __call__(self, y, gemm, group):
+        """``gemm(s, e)`` writes rows [s, e) of ``y`` ([M, N]); returns ``y``
+        all-reduced over ``group``."""
+        M = y.shape[0]
+        if self.chunks <= 1 or M < self.min_rows:
+            gemm(0, M)
+            dist.all_reduce(y, group=group)
+            return y
+        step = -(-M // self.chunks)
+        step = -(-step // 128) * 128  # GEMM-friendly chunk rows
+        prev = torch._C._get_sm_carveout_experimental()
+        use = self.carveout is not None and y.is_cuda
+        if use:
+            torch._C._set_sm_carveout_experimental(int(self.carveout))
+        works = []
+        try:
+            for s in range(0, M, step):
+                e = min(M, s + step)
+                gemm(s, e)
+                works.append(dist.all_reduce(y[s:e], group=group, async_op=True))
+        finally:
+            if use:
+                torch._C._set_sm_carveout_experimental(prev)
+        for w in works:
+            w.wait()
+        return y
 
 
 class RowParallelLinear(torch.nn.Module):
@@ -37,34 +74,48 @@ class RowParallelLinear(torch.nn.Module):
     this rank's input columns ``cols`` of the full layer; the bias enters once,
     through rank 0's GEMM."""
 
-    def __init__(self, full: torch.nn.Linear, cols: torch.Tensor, group, rank):
+    def __init__(self, full: torch.nn.Linear, cols: torch.Tensor, group, rank, overlap=None):
         super().__init__()
         self.weight = _param(full.weight.index_select(1, cols.to(full.weight.device)))
         self.bias = _param(full.bias) if full.bias is not None and rank == 0 else None
         self.group = group
+        self.overlap = overlap or _Overlap(1, None)
 
     def forward(self, x):
-        y = F.linear(x, self.weight, self.bias)
-        dist.all_reduce(y, group=self.group)
-        return y
+        x2 = x.reshape(-1, x.shape[-1])
+        y = torch.empty(x2.shape[0], self.weight.shape[0], dtype=x.dtype, device=x.device)
+        wt = self.weight.t()
+
+        def gemm(s, e):
+            if self.bias is None:
+                torch.mm(x2[s:e], wt, out=y[s:e])
+            else:
+                torch.addmm(self.bias, x2[s:e], wt, out=y[s:e])
+
+        return self.overlap(y, gemm, self.group).view(*x.shape[:-1], -1)
 
 
 class RowParallelJoined(torch.nn.Module):
     """Row-parallel form of ``flux_model.JoinedLinear``: this rank's attention
     columns ``cols_a`` and MLP columns ``cols_m``, partial sums all-reduced."""
 
-    def __init__(self, full, cols_a, cols_m, group, rank):
+    def __init__(self, full, cols_a, cols_m, group, rank, overlap=None):
         super().__init__()
         w = full.weight
         self.weight_a = _param(w.index_select(1, cols_a.to(w.device)))
         self.weight_m = _param(w.index_select(1, (full.split + cols_m).to(w.device)))
         self.bias = _param(full.bias) if full.bias is not None and rank == 0 else None
         self.group = group
+        self.overlap = overlap or _Overlap(1, None)
 
     def forward(self, a, m, ops):
-        y = ops.joined_linear(a, m, self.weight_a, self.weight_m, self.bias)
-        dist.all_reduce(y, group=self.group)
-        return y
+        a2, m2 = a.reshape(-1, a.shape[-1]), m.reshape(-1, m.shape[-1])
+        y = torch.empty(a2.shape[0], self.weight_a.shape[0], dtype=a.dtype, device=a.device)
+
+        def gemm(s, e):
+            ops.joined_linear(a2[s:e], m2[s:e], self.weight_a, self.weight_m, self.bias, out=y[s:e])
+
+        return self.overlap(y, gemm, self.group).view(*a.shape[:-1], -1)
 
 
 def _column(full: torch.nn.Linear, rows: torch.Tensor) -> torch.nn.Linear:
@@ -85,11 +136,15 @@ def _slice(n, rank, world):
     return torch.arange(rank * s, (rank + 1) * s)
 
 
-def shard_flux_model(model, group=None):
+def shard_flux_model(model, group=None, *, chunks=1, carveout=None, min_rows=2048):
     """Split ``model`` (a ``FluxLikeTransformer`` with identical weights on
-    every rank) in place for this rank of ``group``; returns it."""
+    every rank) in place for this rank of ``group``; returns it.  Row-parallel
+    layers over at least ``min_rows`` rows run as ``chunks`` row chunks whose
+    all-reduces overlap the next chunk's GEMM, with ``carveout`` SMs kept free
+    of the GEMMs meanwhile (``chunks=1``: one GEMM, then one all-reduce)."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
+    ov = _Overlap(chunks, carveout, min_rows)
     first = model.double_blocks[0].attn if len(model.double_blocks) else model.single_blocks[0].attn
     heads = first.heads
     head_dim = first.to_q.weight.shape[0] // heads
@@ -100,13 +155,13 @@ def shard_flux_model(model, group=None):
         a = b.attn
         for name in ("to_q", "to_k", "to_v", "add_q_proj", "add_k_proj", "add_v_proj"):
             setattr(a, name, _column(getattr(a, name), head_cols))
-        a.to_out[0] = RowParallelLinear(a.to_out[0], head_cols, group, rank)
-        a.to_add_out = RowParallelLinear(a.to_add_out, head_cols, group, rank)
+        a.to_out[0] = RowParallelLinear(a.to_out[0], head_cols, group, rank, ov)
+        a.to_add_out = RowParallelLinear(a.to_add_out, head_cols, group, rank, ov)
         a.heads = heads // world
         for ff in (b.ff_img, b.ff_txt):
             hid = _slice(ff[0].weight.shape[0], rank, world)
             ff[0] = _column(ff[0], hid)
-            ff[1] = RowParallelLinear(ff[1], hid, group, rank)
+            ff[1] = RowParallelLinear(ff[1], hid, group, rank, ov)
     for b in model.single_blocks:
         a = b.attn
         for name in ("to_q", "to_k", "to_v"):
@@ -114,7 +169,7 @@ def shard_flux_model(model, group=None):
         a.heads = heads // world
         hid = _slice(b.proj_mlp.weight.shape[0], rank, world)
         b.proj_mlp = _column(b.proj_mlp, hid)
-        b.proj_out = RowParallelJoined(b.proj_out, head_cols, hid, group, rank)
+        b.proj_out = RowParallelJoined(b.proj_out, head_cols, hid, group, rank, ov)
     model.tp_world, model.tp_rank = world, rank
     if torch.cuda.is_available() and first.to_q.weight.is_cuda:
         torch.cuda.empty_cache()

@@ -76,8 +76,12 @@ class EagerBlockOps:
         return F.gelu(F.linear(x, weight, bias), approximate="tanh")
 
     @staticmethod
-    def joined_linear(a, m, weight_a, weight_m, bias):
-        return F.linear(torch.cat([a, m], -1), torch.cat([weight_a, weight_m], 1), bias)
+    def joined_linear(a, m, weight_a, weight_m, bias, out=None):
+        y = F.linear(torch.cat([a, m], -1), torch.cat([weight_a, weight_m], 1), bias)
+        if out is None:
+            return y
+        out.copy_(y.reshape(out.shape))
+        return out
 
 
 def _model_and_inputs():
@@ -107,7 +111,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, chunks=1):
     try:
         from hilberta_b200.flux_tp import shard_flux_model
 
@@ -117,7 +121,7 @@ def _worker(rank, world, port, q):
         with torch.no_grad():
             full = model(*x)
             n_full = sum(p.numel() for p in model.parameters())
-            shard_flux_model(model)
+            shard_flux_model(model, chunks=chunks, carveout=None, min_rows=1)
             local = model(*x)
         n_local = sum(p.numel() for p in model.parameters())
         err = float((local - full).abs().max() / full.abs().max())
@@ -129,12 +133,13 @@ def _worker(rank, world, port, q):
         traceback.print_exc()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_tensor_parallel_step_matches_unsharded(world):
+@pytest.mark.parametrize("world,chunks", [(2, 1), (4, 1), (2, 3)])
+def test_tensor_parallel_step_matches_unsharded(world, chunks):
+    """chunks > 1: row-parallel GEMMs in row chunks with async all-reduces."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, chunks)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=180) for _ in procs)

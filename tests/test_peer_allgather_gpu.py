@@ -11,7 +11,6 @@ with the full-head output bit-identical to the per-slice kernel results.
 
 from __future__ import annotations
 
-import ctypes
 import os
 import socket
 import traceback

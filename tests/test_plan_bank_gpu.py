@@ -62,3 +62,24 @@ def test_row_checks(fault, message):
     bad = dataclasses.replace(plan, phases=type(plan.phases)(phases))
     with pytest.raises(ValueError, match=message):
         PlanBank(bad)
+
+
+def test_plan_cache_round_trip_feeds_the_kernel(tmp_path):
+    """A plan built on the GPU, cached on disk and loaded back gives the same
+    manifest, rows and attention output (bit for bit) as the fresh plan."""
+    import hilberta_b200 as hb
+    from hilberta_b200.plan_cache import PlanCache
+
+    cache = PlanCache(tmp_path)
+    fresh = cache.get(4, 1, False, 32)
+    loaded = cache.get(4, 1, False, 32)
+    assert fresh.manifest() == loaded.manifest()
+    for a, b in zip(fresh.phases, loaded.phases):
+        assert torch.equal(a.kv_indices, b.kv_indices) and torch.equal(a.kv_counts, b.kv_counts)
+    g = torch.Generator().manual_seed(9)
+    q, k, v = (torch.randn(1, 2, fresh.total_tokens, 128, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
+    outs = []
+    for plan in (fresh, loaded):
+        meta = hb.PlanBank(plan).on_device(torch.device("cuda"))["paired_phases"][1]
+        outs.append(hb.paired_attention(q, k, v, meta))
+    assert torch.equal(outs[0], outs[1])
