@@ -57,6 +57,7 @@ EXPORTS = (
     "hb_ipc_open",
     "hb_ipc_close",
     "hb_adaln_residual",
+    "hb_expand_kv128",
 )
 
 
@@ -129,6 +130,7 @@ _SIGS = {
     "hb_ipc_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
     "hb_ipc_open": (_I, [_P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
     "hb_ipc_close": (_I, [_P, ctypes.c_uint64]),
+    "hb_expand_kv128": (_I, [_P, _P, _I64, _I, _P, _I, _P, _P, _I64, _P, _P]),
     "hb_adaln_residual": (
         _I,
         [_P, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, ctypes.c_float, _I, _P],

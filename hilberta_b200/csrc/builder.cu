@@ -371,6 +371,50 @@ __global__ void k_pair(const int32_t* __restrict__ ids, int64_t ld, const int32_
     }
 }
 
+// KV128 paired rows -> the equivalent KV64 rows.  A KV128 entry (block b, flag
+// bits half + 2*key_half, paired_metadata.py:26-51) covers 64-key blocks 2b and
+// 2b+1; each half with any query-half bit becomes one KV64 entry whose bits 0/1
+// are that half's.  One warp per paired row; entries stay ascending, so the
+// result is the row pair_metadata builds for key_block_size 64.  Counts are
+// clamped to [0, width]; flag bits above 3 are ignored.
+__global__ void k_expand_kv128(const int32_t* __restrict__ ids, const int32_t* __restrict__ flags, int64_t ld,
+                               int width, const int32_t* __restrict__ counts, int rows, int32_t* __restrict__ out_ids,
+                               int32_t* __restrict__ out_flags, int64_t ld_out, int32_t* __restrict__ out_counts) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int c = min(max(counts[row], 0), width);
+    int base = 0;
+    for (int e0 = 0; e0 < c; e0 += 32) {
+        const int e = e0 + lane;
+        int blk = 0, f = 0;
+        if (e < c) {
+            blk = ids[row * ld + e];
+            f = flags[row * ld + e] & 15;
+        }
+        const int lo = f & 3, hi = (f >> 2) & 3;
+        const int n = (lo != 0) + (hi != 0);
+        int incl = n;  // inclusive warp scan of the entries each lane emits
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        int pos = base + incl - n;
+        if (lo) {
+            out_ids[row * ld_out + pos] = 2 * blk;
+            out_flags[row * ld_out + pos] = lo;
+            pos++;
+        }
+        if (hi) {
+            out_ids[row * ld_out + pos] = 2 * blk + 1;
+            out_flags[row * ld_out + pos] = hi;
+        }
+        base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) out_counts[row] = base;
+}
+
 // Dense token mask, one CTA per 64-row (block_size) query block (plan.py:70-84).
 __global__ void k_dense_mask(const int32_t* __restrict__ ids, int64_t ld, const int32_t* __restrict__ counts, int tokens,
                              int global_tokens, int bs, uint8_t* __restrict__ mask) {
@@ -520,6 +564,19 @@ extern "C" int hb_pair_metadata(const int32_t* kv_indices, int64_t ld, const int
     HB_CUDA_TRY(cudaMemsetAsync(info, 0, sizeof(int32_t), st));
     k_pair<<<rows / 2, 256, smem, st>>>(kv_indices, ld, kv_counts, ratio, nkb, out_ids, out_flags, ld_out, out_counts,
                                         info);
+    HB_LAUNCH_CHECK();
+    return HB_OK;
+}
+
+extern "C" int hb_expand_kv128(const int32_t* kv_indices, const int32_t* kv_flags, int64_t ld, int32_t width,
+                               const int32_t* kv_counts, int32_t rows, int32_t* out_ids, int32_t* out_flags,
+                               int64_t ld_out, int32_t* out_counts, void* stream_) {
+    if (rows < 0 || width < 1 || ld < width || ld_out < 2 * (int64_t)width) return HB_ERR_ARG;
+    if (rows == 0) return HB_OK;
+    if (!kv_indices || !kv_flags || !kv_counts || !out_ids || !out_flags || !out_counts) return HB_ERR_ARG;
+    constexpr int kWarps = 8;
+    k_expand_kv128<<<(rows + kWarps - 1) / kWarps, 32 * kWarps, 0, (cudaStream_t)stream_>>>(
+        kv_indices, kv_flags, ld, width, kv_counts, rows, out_ids, out_flags, ld_out, out_counts);
     HB_LAUNCH_CHECK();
     return HB_OK;
 }

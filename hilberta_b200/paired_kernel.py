@@ -55,8 +55,44 @@ def device_status(device=None, *, clear=True) -> int:
     return bits
 
 
+_kv64_cache = {}
+
+
+def _as_kv64(metadata):
+    """KV64 form of a KV128 paired table (hb_expand_kv128, once per table: the
+    result is cached with the source tensors, keyed by their storage and version
+    counters, so an in-place edit of the table is re-expanded; tables made under
+    inference mode have no version counter and are expanded on every call)."""
+    if metadata.key_block_size == 64:
+        return metadata
+    src = (metadata.kv_indices, metadata.kv_flags, metadata.kv_counts)
+    # inference tensors carry no version counter: expanded on every call instead
+    key = None if any(x.is_inference() for x in src) else tuple((x.data_ptr(), x._version, tuple(x.shape)) for x in src)
+    hit = _kv64_cache.get(key) if key is not None else None
+    if hit is not None:
+        return hit[1]
+    from .paired_metadata import PairedMetadata
+
+    rows, width = metadata.kv_indices.shape
+    dev = metadata.kv_indices.device
+    ids = torch.zeros(rows, 2 * width, dtype=torch.int32, device=dev)
+    flags, counts = torch.zeros_like(ids), torch.zeros(rows, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.lib().hb_expand_kv128(
+            _lib.ptr(metadata.kv_indices), _lib.ptr(metadata.kv_flags), width, width, _lib.ptr(metadata.kv_counts),
+            rows, _lib.ptr(ids), _lib.ptr(flags), 2 * width, _lib.ptr(counts), _lib.stream_ptr(dev))
+    _lib.check(rc, "hb_expand_kv128")
+    meta64 = PairedMetadata(ids, flags, counts, metadata.tokens, metadata.global_tokens, 64)
+    if key is not None:
+        if len(_kv64_cache) >= 16:
+            _kv64_cache.pop(next(iter(_kv64_cache)))
+        _kv64_cache[key] = (src, meta64)  # holding `src` keeps its storage (and key) from being reused
+    return meta64
+
+
 def _launch(q, k, v, out, metadata, N, G, scale, row_map=None, raster=None):
     """The one native call of the attention path."""
+    metadata = _as_kv64(metadata)
     dev = q.device
     stream = torch.cuda.current_stream(dev)
     B, H, _, D = q.shape
@@ -78,13 +114,14 @@ def _launch(q, k, v, out, metadata, N, G, scale, row_map=None, raster=None):
     if rc == _lib.HB_ERR_TMA:
         raise ValueError("Q/K/V need 16-byte aligned base pointers and strides for TMA tiles")
     if rc == _lib.HB_ERR_UNSUPPORTED:
-        raise NotImplementedError(f"paired_attention: {_lib.status_text(rc)} (key_block_size 64, D 64/128)")
+        raise NotImplementedError(f"paired_attention: {_lib.status_text(rc)} (D 64/128)")
     _lib.check(rc, "hb_paired_fwd")
 
 
 def _launch_allgather(q, k, v, full, metadata, N, G, scale, peers):
     """hb_paired_fwd_allgather: `full` is this rank's [B, H_all, N, D] view (its
     strides describe every rank's output); `peers` an _lib.PeerOut."""
+    metadata = _as_kv64(metadata)
     dev = q.device
     stream = torch.cuda.current_stream(dev)
     B, H, _, D = q.shape

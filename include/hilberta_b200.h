@@ -265,6 +265,19 @@ int hb_norm_rope_pack(const void* txt, int64_t txt_sb, int64_t txt_sn, const voi
                       const float* sin, const int32_t* image_rows, void* out, int64_t o_sb,
                       int64_t o_sn, int64_t o_sh, int dtype, int32_t* status, void* stream);
 
+/* ---- KV128 paired metadata -> KV64 -------------------------------------- */
+/* The reference kernel also takes paired metadata with 128-key blocks
+ * (paired_metadata.py:26-51 key_block_size=128: flag bit half + 2*key_half;
+ * paired_kernel.py:65-75).  hb_paired_fwd runs 64-key blocks; this rewrites a
+ * KV128 table [rows][ld] (width used entries per row) into the equivalent KV64
+ * table [rows][ld_out] (ld_out >= 2*width; entries past a row's count are not
+ * written): entry (b, f) becomes (2b, f & 3) and (2b+1, (f >> 2) & 3), each only
+ * when its bits are nonzero, in order.  The result equals pair_metadata with
+ * key_block_size 64 on the same rows, so the attention is the same. */
+int hb_expand_kv128(const int32_t* kv_indices, const int32_t* kv_flags, int64_t ld, int32_t width,
+                    const int32_t* kv_counts, int32_t rows, int32_t* out_ids, int32_t* out_flags,
+                    int64_t ld_out, int32_t* out_counts, void* stream);
+
 /* ---- adaLN modulation and gated residual of the FLUX blocks -------------- */
 /* No counterpart in the reference's own code: the adaLN-Zero steps of the
  * diffusers FLUX blocks that call the attention processor

@@ -179,3 +179,21 @@ def test_adaln_residual_argument_checks(lib):
     assert call(rs=3076) == _lib.HB_ERR_ALIGN
     assert call(rows=0) == _lib.HB_OK
     assert call(y=None, gate=None, x_out=None, rows=0) == _lib.HB_OK  # modulation only
+
+
+def test_expand_kv128_argument_checks(lib):
+    """hb_expand_kv128 checks widths and pointers on the host; zero rows is a no-op."""
+    from hilberta_b200 import _lib
+
+    f = ctypes.c_void_p(1 << 20)
+
+    def call(rows=4, width=8, ld=8, ld_out=16, ids=f, out=f):
+        return lib.hb_expand_kv128(ids, f, ld, width, f, rows, out, f, ld_out, f, None)
+
+    assert call(width=0) == _lib.HB_ERR_ARG
+    assert call(ld=4) == _lib.HB_ERR_ARG  # row stride below the width
+    assert call(ld_out=15) == _lib.HB_ERR_ARG  # room for two KV64 entries per KV128 entry
+    assert call(rows=-1) == _lib.HB_ERR_ARG
+    assert call(ids=None) == _lib.HB_ERR_ARG
+    assert call(out=None) == _lib.HB_ERR_ARG
+    assert call(rows=0, ids=None, out=None) == _lib.HB_OK
