@@ -424,38 +424,35 @@ def prep_side_timing(plan, H, dev, steps=10, D=128):
 def flux_step_timing(a, dev, world, steps=3, warmup=2):
     """One denoising step of a FLUX.1-architecture transformer with random
     weights (19 double + 38 single blocks, hidden 3072, 24 x 128 heads, 512 text
-    tokens; hilberta_b200/flux_model.py) at this config's resolution, with
-    HilbertA attention (the plan's phases, layer i on phase i % 4) in every
-    joint-attention call, against the same weights with dense attention.
-    N > 1: tensor-parallel over the ranks (hilberta_b200/flux_tp.py), each rank
+    tokens; hilberta_b200/flux_model.py) at this config's resolution, run
+    through the reference's adapter entry, ``persistent_flux_attention(model,
+    plan, backend="paired")`` (HilbertA in every joint attention, layer i on
+    phase i % 4, image tokens gathered into the plan's order at entry and back
+    at exit), against the same weights with dense attention outside it.  N > 1:
+    tensor-parallel over the ranks (hilberta_b200/flux_tp.py), each rank
     attending over its 24/N heads; times are the max over ranks.  Inputs are
-    device-resident; the step includes the entry/exit permutation.  The
-    attention parts are timed alone: 57 paired calls (phases cycled) and 57
-    dense SDPA calls on this rank's heads."""
+    device-resident.  The attention parts are timed alone: 57 paired calls
+    (phases cycled) and 57 dense SDPA calls on this rank's heads."""
     import torch.distributed as dist
 
     from hilberta_b200 import PlanBank, bridge_k_plan, paired_attention
-    from hilberta_b200.flux_model import FluxLikeTransformer, parameter_count
+    from hilberta_b200.flux_adapter import persistent_flux_attention
+    from hilberta_b200.flux_model import FluxTransformer, parameter_count, step_inputs
 
     res_px, tiles, k = CONFIGS[a.config]
     grid = res_px // 16
     plan = bridge_k_plan(tiles, k, False, grid_size=grid)
-    bank = PlanBank(plan)
     torch.manual_seed(5)  # identical weights on every rank
-    model = FluxLikeTransformer(grid, bank, attention="hilberta", device=dev)
+    model = FluxTransformer(device=dev)
     params = parameter_count(model)
     if world > 1:
         from hilberta_b200.flux_tp import shard_flux_model
 
         shard_flux_model(model, chunks=a.tp_chunks, carveout=a.tp_carveout or None)
-    g = torch.Generator(device="cpu").manual_seed(6)
-    latents = torch.randn(1, grid * grid, 64, generator=g).to(torch.bfloat16).to(dev)
-    text = torch.randn(1, plan.text_tokens, 4096, generator=g).to(torch.bfloat16).to(dev)
-    pooled = torch.randn(1, 768, generator=g).to(torch.bfloat16).to(dev)
-    t, guid = torch.tensor([0.75], device=dev), torch.tensor([3.5], device=dev)
+    x = step_inputs(grid, plan.text_tokens, dev)
     N, hr = plan.total_tokens, 24 // world
     qkv = [torch.randn(1, hr, N, 128, device=dev, dtype=torch.bfloat16) for _ in range(3)]
-    metas = bank.on_device(dev)["paired_phases"]
+    metas = PlanBank(plan).on_device(dev)["paired_phases"]
 
     def timed(fn, n):
         for _ in range(warmup):
@@ -473,10 +470,11 @@ def flux_step_timing(a, dev, world, steps=3, warmup=2):
 
     times, outs = {}, {}
     with torch.inference_mode():
-        for mode in ("hilberta", "dense"):
-            model.set_attention(mode)
-            times[f"{mode}_ms"] = timed(lambda: model(latents, text, pooled, t, guid), steps)
-            outs[mode] = model(latents, text, pooled, t, guid).float()
+        with persistent_flux_attention(model, plan, backend="paired") as info:
+            times["hilberta_ms"] = timed(lambda: model(**x), steps)
+            outs["hilberta"] = model(**x).sample.float()
+        times["dense_ms"] = timed(lambda: model(**x), steps)
+        outs["dense"] = model(**x).sample.float()
         times["attention_ms_hilberta"] = timed(lambda: [paired_attention(*qkv, metas[i % 4]) for i in range(57)], 1)
         times["attention_ms_dense"] = timed(
             lambda: [torch.nn.functional.scaled_dot_product_attention(*qkv) for _ in range(57)], 1)
@@ -485,12 +483,14 @@ def flux_step_timing(a, dev, world, steps=3, warmup=2):
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     res = {"workload": f"FLUX.1-architecture step, {a.config}, 19+38 blocks, hidden 3072, random weights",
            "parameters": params,
+           "entry": "persistent_flux_attention(model, plan, backend='paired')",
            "parallelism": f"tensor-parallel x{world} (heads and MLP hidden sharded, NCCL all-reduce; "
            f"{a.tp_chunks} row chunks per row-parallel GEMM, {a.tp_carveout} SMs carved out)"
            if world > 1 else "single GPU"}
-    res.update({key: round(float(x), 2) for key, x in zip(times, vals)})
+    res.update({key: round(float(v), 2) for key, v in zip(times, vals)})
     res["speedup"] = round(res["dense_ms"] / res["hilberta_ms"], 3)
     res["rel_diff_vs_dense"] = round(float((outs["hilberta"] - outs["dense"]).norm() / outs["dense"].norm()), 4)
+    res["adapter_calls"] = {k: info[k] for k in ("transformer_calls", "image_reorder_calls", "image_inverse_calls")}
     res["note"] = ("steps=%d warmup=%d, device-resident inputs, max over ranks; attention_ms_* = 57 calls on this "
                    "rank's heads; rel_diff_vs_dense is the sparse step's relative L2 distance from the dense step "
                    "(a property of the sparse pattern, not an error)" % (steps, warmup))

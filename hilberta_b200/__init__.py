@@ -11,9 +11,10 @@ plan cache (``PlanBank``), plans on disk (``save_plan``, ``load_plan``,
 ``PlanCache``), the processor's Q/K/V preparation
 (``prepare_qkv``), and head-parallel attention over several GPUs with the head
 all-gather fused into the kernel (``PeerAllGather``), and the FLUX processor
-built from them (``HilbertAProcessor``), and a FLUX.1-architecture transformer
-with random weights that runs a denoising step on it (``FluxLikeTransformer``,
-imported from ``hilberta_b200.flux_model``).
+built from them (``HilbertAProcessor``), the reference adapter's entry
+(``persistent_flux_attention``), and a FLUX.1-architecture transformer with
+random weights and diffusers' interface to run it on
+(``hilberta_b200.flux_model.FluxTransformer``).
 """
 
 from .bridge_k import bridge_k_plan
@@ -25,6 +26,7 @@ from .plan_bank import PlanBank
 from .plan_cache import PlanCache, load_plan, save_plan
 from .prep import norm_rope_pack, prepare_qkv
 from .processor import HilbertAProcessor
+from .flux_adapter import persistent_flux_attention
 from .sparse_kernel import explicit_mask, validate_metadata
 
 __version__ = "0.1.0"
@@ -55,4 +57,5 @@ __all__ = [
     "all_gather_heads",
     "head_parallel_attention",
     "HilbertAProcessor",
+    "persistent_flux_attention",
 ]

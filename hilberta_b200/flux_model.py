@@ -10,11 +10,15 @@ for text and image tokens, one joint attention), 38 single-stream blocks
 embedding, tanh-GELU MLPs with ratio 4.  Weights are random (no checkpoint is
 available); the step's cost and data flow are the model's.
 
-Attention runs through ``HilbertAProcessor`` (fused Q/K/V preparation + paired
-block-sparse attention on the layer's phase) or, for the comparison, the same
-prepared Q/K/V through dense scaled-dot-product attention.  Image tokens are
-permuted into the plan's physical order once per step at entry and back at exit
-(the reference's sampling layout, hilberta/sampling_layout.py:88-116).
+``FluxTransformer`` carries the module names and the forward signature of
+diffusers' ``FluxTransformer2DModel`` (``transformer_blocks``,
+``single_transformer_blocks``, ``attn.set_processor``; ``forward(hidden_states,
+encoder_hidden_states, pooled_projections, timestep, img_ids, txt_ids, guidance,
+...)``, rotary tables from the position ids), so the reference's adapter entry,
+``flux_adapter.persistent_flux_attention``, applies to it unchanged.  Outside
+that context every joint attention is dense (``DenseProcessor``: the fused Q/K/V
+preparation and torch SDPA); inside it, ``HilbertAProcessor`` on the layer's
+phase with the image tokens permuted into the plan's order once per call.
 """
 
 from __future__ import annotations
@@ -24,7 +28,6 @@ import torch.nn.functional as F
 
 from .block_ops import NativeBlockOps
 from .prep import norm_rope_pack
-from .processor import HilbertAProcessor
 
 
 class RMSNormWeight(torch.nn.Module):
@@ -61,6 +64,9 @@ class JointAttention(torch.nn.Module):
             self.to_out = torch.nn.ModuleList([_linear(inner, dim, dtype, device), torch.nn.Dropout(0.0)])
             self.to_add_out = _linear(inner, dim, dtype, device)
         self.processor = None
+
+    def set_processor(self, processor):
+        self.processor = processor
 
     def forward(self, hidden_states, encoder_hidden_states=None, image_rotary_emb=None):
         return self.processor(self, hidden_states, encoder_hidden_states, image_rotary_emb=image_rotary_emb)
@@ -194,81 +200,81 @@ def rotary_3axis(ids, axes=(16, 56, 56), theta=10000.0):
     return torch.cat(cos, 1).float().contiguous(), torch.cat(sin, 1).float().contiguous()
 
 
-class FluxLikeTransformer(torch.nn.Module):
-    """``forward(latents [B, n, 64], text [B, T, text_dim], pooled [B, 768],
-    timestep [B], guidance [B] or None)`` -> ``[B, n, 64]`` for a ``grid x grid``
-    image in raster order.
+class FluxOutput:
+    """Prediction of one call (``.sample``), like diffusers'
+    ``Transformer2DModelOutput``."""
 
-    ``attention``: "hilberta" (``HilbertAProcessor`` on ``bank``), "dense" (all
-    tokens), or "masked" (dense attention under ``bank``'s phase masks).  With a
-    bank, image tokens run in the plan's physical order whatever the attention;
-    ``set_attention`` switches processors on the same weights.  ``block_ops``
-    (default ``NativeBlockOps``: the library's adaLN kernels and cuBLASLt
-    epilogues) runs the blocks' modulation, residual and MLP steps."""
+    def __init__(self, sample):
+        self.sample = sample
 
-    def __init__(self, grid, bank=None, attention="hilberta", num_double=19, num_single=38, dim=3072, heads=24,
-                 head_dim=128, in_channels=64, text_dim=4096, pooled_dim=768, text_tokens=512, dtype=torch.bfloat16, device="cuda",
-                 kernel_options=None, block_ops=None):
+
+class FluxTransformer(torch.nn.Module):
+    """FLUX.1 transformer with random weights (defaults: FLUX.1-dev's sizes,
+    11.90 B parameters) and diffusers' ``FluxTransformer2DModel`` interface.
+
+    ``forward(hidden_states [B, n, 64], encoder_hidden_states [B, T, text_dim],
+    pooled_projections [B, pooled_dim], timestep [B], img_ids [n, 3],
+    txt_ids [T, 3], guidance [B] or None, joint_attention_kwargs=None,
+    controlnet_block_samples=None, controlnet_single_block_samples=None,
+    return_dict=True)`` -> ``FluxOutput`` (or a 1-tuple).  Tokens are processed in
+    the order given; the rotary tables follow the ids.  ``block_ops`` (default
+    ``NativeBlockOps``: the library's adaLN kernels and cuBLASLt epilogues) runs
+    the blocks' modulation, residual and MLP steps."""
+
+    def __init__(self, num_double=19, num_single=38, dim=3072, heads=24, head_dim=128, in_channels=64, text_dim=4096,
+                 pooled_dim=768, axes=(16, 56, 56), dtype=torch.bfloat16, device="cuda", block_ops=None):
         super().__init__()
+        if sum(axes) != head_dim:
+            raise ValueError("rotary axes must add up to head_dim")
         self.ops = NativeBlockOps() if block_ops is None else block_ops
-        self.grid, self.bank = grid, bank
+        self.axes = tuple(int(a) for a in axes)
         self.x_embedder = _linear(in_channels, dim, dtype, device)
         self.context_embedder = _linear(text_dim, dim, dtype, device)
-        self.cond = ConditioningEmbedder(dim, pooled_dim, dtype, device)
-        self.double_blocks = torch.nn.ModuleList(DoubleStreamBlock(dim, heads, head_dim, dtype, device) for _ in range(num_double))
-        self.single_blocks = torch.nn.ModuleList(SingleStreamBlock(dim, heads, head_dim, dtype, device) for _ in range(num_single))
-        self.mod_out = _linear(dim, 2 * dim, dtype, device)
+        self.time_text_embed = ConditioningEmbedder(dim, pooled_dim, dtype, device)
+        self.transformer_blocks = torch.nn.ModuleList(
+            DoubleStreamBlock(dim, heads, head_dim, dtype, device) for _ in range(num_double))
+        self.single_transformer_blocks = torch.nn.ModuleList(
+            SingleStreamBlock(dim, heads, head_dim, dtype, device) for _ in range(num_single))
+        self.norm_out = _linear(dim, 2 * dim, dtype, device)
         self.proj_out = _linear(dim, in_channels, dtype, device)
-        self.kernel_options = kernel_options
-        self.set_attention(attention)
-        # positions: text (0, 0, 0); image (0, row, col), in the token order the step uses
-        g = grid
-        rows = torch.arange(g * g, device=device) // g
-        cols = torch.arange(g * g, device=device) % g
-        img_ids = torch.stack([torch.zeros_like(rows), rows, cols], dim=1)
-        self.order = self.inverse = None
-        if bank is not None:
-            if bank.image_tokens != g * g:
-                raise ValueError("The plan's image-token count does not match the grid")
-            entry = bank.on_device(torch.device(device))
-            self.order, self.inverse = entry["order"], entry["inverse"]
-            img_ids = img_ids.index_select(0, self.order)
-        self.text_tokens = bank.text_tokens if bank is not None else text_tokens
-        ids = torch.cat([torch.zeros(self.text_tokens, 3, dtype=img_ids.dtype, device=device), img_ids])
-        self.rot = rotary_3axis(ids)
+        self.gradient_checkpointing = False
+        self.eval()
+        for m in self.attention_modules():
+            m.set_processor(DenseProcessor())
 
-    def set_attention(self, attention):
-        if attention not in ("hilberta", "dense", "masked"):
-            raise ValueError("attention must be 'hilberta', 'dense' or 'masked'")
-        if attention != "dense" and self.bank is None:
-            raise ValueError(f"attention={attention!r} needs a PlanBank")
-        attn_modules = [b.attn for b in self.double_blocks] + [b.attn for b in self.single_blocks]
-        for layer, m in enumerate(attn_modules):
-            if attention == "hilberta":
-                m.processor = HilbertAProcessor(self.bank, layer, self.kernel_options)
-            else:
-                m.processor = DenseProcessor(self.bank if attention == "masked" else None, layer)
-        self.attention = attention
+    def attention_modules(self):
+        return [b.attn for b in self.transformer_blocks] + [b.attn for b in self.single_transformer_blocks]
 
-    def forward(self, latents, text, pooled, timestep, guidance=None):
-        if latents.shape[1] != self.grid * self.grid or text.shape[1] != self.text_tokens:
-            raise ValueError("latent or text token count does not match the model")
-        if self.order is not None:  # into the plan's physical order, once per step
-            latents = latents.index_select(1, self.order)
-        temb = self.cond(timestep, guidance, pooled)
-        img = self.x_embedder(latents)
-        txt = self.context_embedder(text)
-        for b in self.double_blocks:
-            img, txt = b(img, txt, temb, self.rot, self.ops)
+    def forward(self, hidden_states, encoder_hidden_states=None, pooled_projections=None, timestep=None, img_ids=None,
+                txt_ids=None, guidance=None, joint_attention_kwargs=None, controlnet_block_samples=None,
+                controlnet_single_block_samples=None, return_dict=True):
+        if controlnet_block_samples is not None or controlnet_single_block_samples is not None:
+            raise ValueError("ControlNet residuals are not supported")
+        if txt_ids.ndim == 3:
+            txt_ids = txt_ids[0]
+        if img_ids.ndim == 3:
+            img_ids = img_ids[0]
+        if img_ids.shape[0] != hidden_states.shape[1] or txt_ids.shape[0] != encoder_hidden_states.shape[1]:
+            raise ValueError("position ids do not match the token counts")
+        rot = rotary_3axis(torch.cat([txt_ids, img_ids], 0), self.axes)
+        temb = self.time_text_embed(timestep, guidance, pooled_projections)
+        img = self.x_embedder(hidden_states)
+        txt = self.context_embedder(encoder_hidden_states)
+        for b in self.transformer_blocks:
+            img, txt = b(img, txt, temb, rot, self.ops)
         x = torch.cat([txt, img], dim=1)
-        for b in self.single_blocks:
-            x = b(x, temb, self.rot, self.ops)
+        for b in self.single_transformer_blocks:
+            x = b(x, temb, rot, self.ops)
         img = x[:, txt.shape[1]:]
-        shift, scale = self.mod_out(F.silu(temb)).chunk(2, dim=-1)
+        shift, scale = self.norm_out(F.silu(temb)).chunk(2, dim=-1)
         out = self.proj_out(_modulate(img, shift, scale))
-        if self.order is not None:
-            out = out.index_select(1, self.inverse)
-        return out
+        return FluxOutput(out) if return_dict else (out,)
+
+
+def image_ids(grid, device=None):
+    """Position ids [grid*grid, 3] of a raster image: (0, row, column)."""
+    r = torch.arange(grid * grid, device=device)
+    return torch.stack([torch.zeros_like(r), r // grid, r % grid], dim=1)
 
 
 def parameter_count(model) -> int:
@@ -285,17 +291,20 @@ def attention_flops_per_step(bank, heads=24, head_dim=128, layers=57):
     return total
 
 
-__all__ = ["FluxLikeTransformer", "DenseProcessor", "JoinedLinear", "ConditioningEmbedder", "timestep_features", "rotary_3axis", "parameter_count", "attention_flops_per_step"]
+__all__ = ["FluxTransformer", "FluxOutput", "DenseProcessor", "JoinedLinear", "ConditioningEmbedder", "timestep_features",
+           "image_ids", "step_inputs", "rotary_3axis", "parameter_count", "attention_flops_per_step"]
 
 
 def _main(argv=None):
     """``python -m hilberta_b200.flux_model [--grid 128] [--tiles 16] [--k 3]
-    [--steps 3] [--profile]``: time one step with HilbertA and dense attention on
-    cuda:0 and, with ``--profile``, print the per-kernel device times of one
-    HilbertA step (torch.profiler)."""
+    [--steps 3] [--profile]``: time one step with HilbertA attention
+    (``persistent_flux_attention(..., backend="paired")``) and with dense
+    attention on cuda:0 and, with ``--profile``, print the per-kernel device
+    times of one HilbertA step (torch.profiler)."""
     import argparse
 
-    from . import PlanBank, bridge_k_plan
+    from .bridge_k import bridge_k_plan
+    from .flux_adapter import persistent_flux_attention
 
     ap = argparse.ArgumentParser()
     ap.add_argument("--grid", type=int, default=128)
@@ -307,33 +316,47 @@ def _main(argv=None):
     dev = torch.device("cuda", 0)
     plan = bridge_k_plan(a.tiles, a.k, False, grid_size=a.grid)
     torch.manual_seed(5)
-    model = FluxLikeTransformer(a.grid, PlanBank(plan), attention="hilberta", device=dev)
-    g = torch.Generator().manual_seed(6)
-    x = (torch.randn(1, a.grid * a.grid, 64, generator=g).to(torch.bfloat16).to(dev),
-         torch.randn(1, plan.text_tokens, 4096, generator=g).to(torch.bfloat16).to(dev),
-         torch.randn(1, 768, generator=g).to(torch.bfloat16).to(dev),
-         torch.tensor([0.75], device=dev), torch.tensor([3.5], device=dev))
-    with torch.inference_mode():
-        for mode in ("hilberta", "dense"):
-            model.set_attention(mode)
-            for _ in range(2):
-                model(*x)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(a.steps):
-                model(*x)
-            e1.record()
-            torch.cuda.synchronize()
-            print(f"{mode}: {e0.elapsed_time(e1) / a.steps:.2f} ms/step")
-        if a.profile:
-            from torch.profiler import ProfilerActivity, profile
+    model = FluxTransformer(device=dev)
+    x = step_inputs(a.grid, plan.text_tokens, dev)
 
-            model.set_attention("hilberta")
-            with profile(activities=[ProfilerActivity.CUDA]) as p:
-                model(*x)
-                torch.cuda.synchronize()
+    def timed():
+        for _ in range(2):
+            model(**x)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            model(**x)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps
+
+    with torch.inference_mode():
+        with persistent_flux_attention(model, plan, backend="paired"):
+            print(f"hilberta: {timed():.2f} ms/step")
+            if a.profile:
+                from torch.profiler import ProfilerActivity, profile
+
+                with profile(activities=[ProfilerActivity.CUDA]) as p:
+                    model(**x)
+                    torch.cuda.synchronize()
+        print(f"dense: {timed():.2f} ms/step")
+        if a.profile:
             print(p.key_averages().table(sort_by="cuda_time_total", row_limit=20, max_name_column_width=70))
+
+
+def step_inputs(grid, text_tokens, device, batch=1, seed=6, text_dim=4096, pooled_dim=768, dtype=torch.bfloat16):
+    """Seeded synthetic inputs of one denoising call, as keyword arguments."""
+    g = torch.Generator().manual_seed(seed)
+    return dict(
+        hidden_states=torch.randn(batch, grid * grid, 64, generator=g).to(dtype).to(device),
+        encoder_hidden_states=torch.randn(batch, text_tokens, text_dim, generator=g).to(dtype).to(device),
+        pooled_projections=torch.randn(batch, pooled_dim, generator=g).to(dtype).to(device),
+        timestep=torch.full((batch,), 0.75, device=device),
+        img_ids=image_ids(grid, device),
+        txt_ids=torch.zeros(text_tokens, 3, dtype=torch.int64, device=device),
+        guidance=torch.full((batch,), 3.5, device=device),
+    )
 
 
 if __name__ == "__main__":

@@ -1,6 +1,6 @@
 """Tensor-parallel FLUX.1-architecture step over P ranks (one per GPU).
 
-The model of ``flux_model.FluxLikeTransformer`` is split the Megatron way,
+The model of ``flux_model.FluxTransformer`` is split the Megatron way,
 head-aligned so that every rank runs HilbertA attention on its own heads
 (``heads / P`` of them) with the replicated plan metadata:
 
@@ -137,7 +137,7 @@ def _slice(n, rank, world):
 
 
 def shard_flux_model(model, group=None, *, chunks=1, carveout=None, min_rows=2048):
-    """Split ``model`` (a ``FluxLikeTransformer`` with identical weights on
+    """Split ``model`` (a ``FluxTransformer`` with identical weights on
     every rank) in place for this rank of ``group``; returns it.  Row-parallel
     layers over at least ``min_rows`` rows run as ``chunks`` row chunks whose
     all-reduces overlap the next chunk's GEMM, with ``carveout`` SMs kept free
@@ -145,13 +145,13 @@ def shard_flux_model(model, group=None, *, chunks=1, carveout=None, min_rows=204
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     ov = _Overlap(chunks, carveout, min_rows)
-    first = model.double_blocks[0].attn if len(model.double_blocks) else model.single_blocks[0].attn
+    first = (model.transformer_blocks or model.single_transformer_blocks)[0].attn
     heads = first.heads
     head_dim = first.to_q.weight.shape[0] // heads
     if heads % world:
         raise ValueError("heads must split evenly over the ranks")
     head_cols = _slice(heads * head_dim, rank, world)  # this rank's heads, contiguous
-    for b in model.double_blocks:
+    for b in model.transformer_blocks:
         a = b.attn
         for name in ("to_q", "to_k", "to_v", "add_q_proj", "add_k_proj", "add_v_proj"):
             setattr(a, name, _column(getattr(a, name), head_cols))
@@ -162,7 +162,7 @@ def shard_flux_model(model, group=None, *, chunks=1, carveout=None, min_rows=204
             hid = _slice(ff[0].weight.shape[0], rank, world)
             ff[0] = _column(ff[0], hid)
             ff[1] = RowParallelLinear(ff[1], hid, group, rank, ov)
-    for b in model.single_blocks:
+    for b in model.single_transformer_blocks:
         a = b.attn
         for name in ("to_q", "to_k", "to_v"):
             setattr(a, name, _column(getattr(a, name), head_cols))

@@ -85,23 +85,17 @@ class EagerBlockOps:
 
 
 def _model_and_inputs():
-    from hilberta_b200.flux_model import FluxLikeTransformer
+    from hilberta_b200.flux_model import FluxTransformer, image_ids
 
     torch.manual_seed(0)
-    model = FluxLikeTransformer(8, None, attention="dense", num_double=2, num_single=2, dim=128, heads=4,
-                                head_dim=32, text_dim=48, pooled_dim=16, text_tokens=16, dtype=torch.float32,
-                                device="cpu", block_ops=EagerBlockOps())
-    # 2-D axes of the rotary table scaled to head_dim 32
-    from hilberta_b200.flux_model import rotary_3axis
-
+    model = FluxTransformer(num_double=2, num_single=2, dim=128, heads=4, head_dim=32, text_dim=48, pooled_dim=16,
+                            axes=(8, 12, 12), dtype=torch.float32, device="cpu", block_ops=EagerBlockOps())
+    for m in model.attention_modules():
+        m.set_processor(TorchProcessor())
     g = torch.Generator().manual_seed(1)
-    ids = torch.cat([torch.zeros(16, 3, dtype=torch.int64),
-                     torch.stack([torch.zeros(64, dtype=torch.int64), torch.arange(64) // 8, torch.arange(64) % 8], 1)])
-    model.rot = rotary_3axis(ids, axes=(8, 12, 12))
-    for m in [b.attn for b in model.double_blocks] + [b.attn for b in model.single_blocks]:
-        m.processor = TorchProcessor()
-    x = (torch.randn(2, 64, 64, generator=g), torch.randn(2, 16, 48, generator=g), torch.randn(2, 16, generator=g),
-         torch.tensor([0.2, 0.7]), torch.tensor([3.5, 2.0]))
+    x = dict(hidden_states=torch.randn(2, 64, 64, generator=g), encoder_hidden_states=torch.randn(2, 16, 48, generator=g),
+             pooled_projections=torch.randn(2, 16, generator=g), timestep=torch.tensor([0.2, 0.7]),
+             img_ids=image_ids(8), txt_ids=torch.zeros(16, 3, dtype=torch.int64), guidance=torch.tensor([3.5, 2.0]))
     return model, x
 
 
@@ -119,13 +113,13 @@ def _worker(rank, world, port, q, chunks=1):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
         model, x = _model_and_inputs()
         with torch.no_grad():
-            full = model(*x)
+            full = model(**x).sample
             n_full = sum(p.numel() for p in model.parameters())
             shard_flux_model(model, chunks=chunks, carveout=None, min_rows=1)
-            local = model(*x)
+            local = model(**x).sample
         n_local = sum(p.numel() for p in model.parameters())
         err = float((local - full).abs().max() / full.abs().max())
-        ok = err < 1e-5 and model.double_blocks[0].attn.heads == 4 // world and n_local < n_full
+        ok = err < 1e-5 and model.transformer_blocks[0].attn.heads == 4 // world and n_local < n_full
         q.put((rank, "ok" if ok else f"mismatch {err}"))
         dist.destroy_process_group()
     except Exception as e:

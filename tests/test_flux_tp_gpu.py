@@ -1,6 +1,7 @@
 """Tensor-parallel FLUX.1-architecture step on two GPUs (NCCL): each rank runs
-HilbertA attention on its half of the heads inside the sharded blocks, and the
-step's output matches the unsharded HilbertA step of the same weights."""
+HilbertA attention (persistent_flux_attention, backend "paired") on its half of
+the heads inside the sharded blocks, and the step's output matches the
+unsharded HilbertA step of the same weights."""
 
 from __future__ import annotations
 
@@ -26,7 +27,7 @@ def _port():
 def _worker(rank, world, port, q):
     try:
         import hilberta_b200 as hb
-        from hilberta_b200.flux_model import FluxLikeTransformer
+        from hilberta_b200.flux_model import FluxTransformer, step_inputs
         from hilberta_b200.flux_tp import shard_flux_model
 
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -34,21 +35,16 @@ def _worker(rank, world, port, q):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
         plan = hb.bridge_k_plan(4, 1, False, grid_size=32)
-        bank = hb.PlanBank(plan)
         torch.manual_seed(0)
-        model = FluxLikeTransformer(32, bank, attention="hilberta", num_double=2, num_single=2, dim=512, heads=4,
-                                    text_dim=64, pooled_dim=32, device=dev)
-        g = torch.Generator().manual_seed(3)
-        x = (torch.randn(1, 1024, 64, generator=g).to(torch.bfloat16).to(dev),
-             torch.randn(1, plan.text_tokens, 64, generator=g).to(torch.bfloat16).to(dev),
-             torch.randn(1, 32, generator=g).to(torch.bfloat16).to(dev),
-             torch.tensor([0.4], device=dev), torch.tensor([3.5], device=dev))
-        with torch.inference_mode():
-            full = model(*x).float()
-            shard_flux_model(model)
-            local = model(*x).float()
+        model = FluxTransformer(num_double=2, num_single=2, dim=512, heads=4, text_dim=64, pooled_dim=32, device=dev)
+        x = step_inputs(32, plan.text_tokens, dev, seed=3, text_dim=64, pooled_dim=32)
+        with torch.inference_mode(), hb.persistent_flux_attention(model, plan, backend="paired"):
+            full = model(**x).sample.float()
+        shard_flux_model(model)
+        with torch.inference_mode(), hb.persistent_flux_attention(model, plan, backend="paired"):
+            local = model(**x).sample.float()
         rel = float((local - full).norm() / full.norm())
-        heads_ok = all(b.attn.heads == 4 // world for b in model.single_blocks)
+        heads_ok = all(b.attn.heads == 4 // world for b in model.single_transformer_blocks)
         status = hb.device_status(dev)
         q.put((rank, "ok" if rel < 2e-2 and heads_ok and status == 0 else f"rel {rel} heads {heads_ok} st {status}"))
         dist.barrier()
