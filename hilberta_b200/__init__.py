@@ -12,7 +12,8 @@ plan cache (``PlanBank``), plans on disk (``save_plan``, ``load_plan``,
 (``prepare_qkv``), and head-parallel attention over several GPUs with the head
 all-gather fused into the kernel (``PeerAllGather``), and the FLUX processor
 built from them (``HilbertAProcessor``), the reference adapter's entry
-(``persistent_flux_attention``), and a FLUX.1-architecture transformer with
+(``persistent_flux_attention``) and sampling wrapper (``sample_flux_persistent``),
+and a FLUX.1-architecture transformer with
 random weights and diffusers' interface to run it on
 (``hilberta_b200.flux_model.FluxTransformer``).
 """
@@ -27,6 +28,7 @@ from .plan_cache import PlanCache, load_plan, save_plan
 from .prep import norm_rope_pack, prepare_qkv
 from .processor import HilbertAProcessor
 from .flux_adapter import persistent_flux_attention
+from .sampling_layout import sample_flux_persistent
 from .sparse_kernel import explicit_mask, validate_metadata
 
 __version__ = "0.1.0"
@@ -58,4 +60,5 @@ __all__ = [
     "head_parallel_attention",
     "HilbertAProcessor",
     "persistent_flux_attention",
+    "sample_flux_persistent",
 ]
