@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--tp-chunks", type=int, default=1,
                     help="FLUX step at N > 1: row chunks of each row-parallel GEMM (all-reduce overlap)")
     ap.add_argument("--tp-carveout", type=int, default=0, help="SMs kept free of those GEMMs for the all-reduce")
+    ap.add_argument("--tp-sp", type=int, default=0, choices=(0, 1),
+                    help="FLUX step at N > 1: sequence parallelism (token-split streams, all-gather/reduce-scatter)")
     ap.add_argument("--no-flux-step", action="store_true",
                     help="skip the FLUX.1-architecture denoising step (random weights), HilbertA vs dense attention")
     return ap.parse_args()
@@ -448,7 +450,7 @@ def flux_step_timing(a, dev, world, steps=3, warmup=2):
     if world > 1:
         from hilberta_b200.flux_tp import shard_flux_model
 
-        shard_flux_model(model, chunks=a.tp_chunks, carveout=a.tp_carveout or None)
+        shard_flux_model(model, chunks=a.tp_chunks, carveout=a.tp_carveout or None, sequence_parallel=bool(a.tp_sp))
     x = step_inputs(grid, plan.text_tokens, dev)
     N, hr = plan.total_tokens, 24 // world
     qkv = [torch.randn(1, hr, N, 128, device=dev, dtype=torch.bfloat16) for _ in range(3)]
@@ -484,8 +486,10 @@ def flux_step_timing(a, dev, world, steps=3, warmup=2):
     res = {"workload": f"FLUX.1-architecture step, {a.config}, 19+38 blocks, hidden 3072, random weights",
            "parameters": params,
            "entry": "persistent_flux_attention(model, plan, backend='paired')",
-           "parallelism": f"tensor-parallel x{world} (heads and MLP hidden sharded, NCCL all-reduce; "
-           f"{a.tp_chunks} row chunks per row-parallel GEMM, {a.tp_carveout} SMs carved out)"
+           "parallelism": (f"tensor-parallel x{world} (heads and MLP hidden sharded; "
+                           + ("sequence-parallel streams, NCCL all-gather / reduce-scatter)" if a.tp_sp else
+                              f"NCCL all-reduce, {a.tp_chunks} row chunks per row-parallel GEMM, "
+                              f"{a.tp_carveout} SMs carved out)"))
            if world > 1 else "single GPU"}
     res.update({key: round(float(v), 2) for key, v in zip(times, vals)})
     res["speedup"] = round(res["dense_ms"] / res["hilberta_ms"], 3)

@@ -106,6 +106,10 @@ class DenseProcessor:
         return attn.to_out[1](attn.to_out[0](image)), attn.to_add_out(text)
 
 
+def _same(x):
+    return x
+
+
 def _modulate(x, shift, scale):
     """adaLN of the output layer (once per step, eager)."""
     return F.layer_norm(x, x.shape[-1:], eps=1e-6) * (1 + scale[:, None]) + shift[:, None]
@@ -134,13 +138,15 @@ class DoubleStreamBlock(torch.nn.Module):
         self.ff_img = torch.nn.ModuleList([_linear(dim, 4 * dim, dtype, device), _linear(4 * dim, dim, dtype, device)])
         self.ff_txt = torch.nn.ModuleList([_linear(dim, 4 * dim, dtype, device), _linear(4 * dim, dim, dtype, device)])
 
-    def forward(self, img, txt, temb, rot, ops):
+    def forward(self, img, txt, temb, rot, ops, gather=_same):
+        """``gather``: token all-gather of the image stream before its
+        projections (sequence parallelism; identity otherwise)."""
         mi = self.mod_img(F.silu(temb)).chunk(6, dim=-1)
         mt = self.mod_txt(F.silu(temb)).chunk(6, dim=-1)
-        a_img, a_txt = self.attn(ops.modulate(img, mi[0], mi[1]), ops.modulate(txt, mt[0], mt[1]), rot)
+        a_img, a_txt = self.attn(gather(ops.modulate(img, mi[0], mi[1])), ops.modulate(txt, mt[0], mt[1]), rot)
         img, h_img = ops.gate_add_modulate(img, a_img, mi[2], mi[3], mi[4])
         txt, h_txt = ops.gate_add_modulate(txt, a_txt, mt[2], mt[3], mt[4])
-        f_img = self.ff_img[1](ops.linear_gelu(h_img, self.ff_img[0].weight, self.ff_img[0].bias))
+        f_img = self.ff_img[1](ops.linear_gelu(gather(h_img), self.ff_img[0].weight, self.ff_img[0].bias))
         f_txt = self.ff_txt[1](ops.linear_gelu(h_txt, self.ff_txt[0].weight, self.ff_txt[0].bias))
         return ops.gate_add(img, f_img, mi[5]), ops.gate_add(txt, f_txt, mt[5])
 
@@ -153,9 +159,9 @@ class SingleStreamBlock(torch.nn.Module):
         self.proj_mlp = _linear(dim, 4 * dim, dtype, device)
         self.proj_out = JoinedLinear(heads * head_dim, 4 * dim, dim, dtype, device)
 
-    def forward(self, x, temb, rot, ops):
+    def forward(self, x, temb, rot, ops, gather=_same):
         shift, scale, gate = self.mod(F.silu(temb)).chunk(3, dim=-1)
-        h = ops.modulate(x, shift, scale)
+        h = gather(ops.modulate(x, shift, scale))
         mlp = ops.linear_gelu(h, self.proj_mlp.weight, self.proj_mlp.bias)
         a = self.attn(h, None, rot)
         return ops.gate_add(x, self.proj_out(a, mlp, ops), gate)
@@ -238,6 +244,7 @@ class FluxTransformer(torch.nn.Module):
         self.norm_out = _linear(dim, 2 * dim, dtype, device)
         self.proj_out = _linear(dim, in_channels, dtype, device)
         self.gradient_checkpointing = False
+        self.sequence_parallel = None  # flux_tp.TokenShards when the blocks' streams are sharded by tokens
         self.eval()
         for m in self.attention_modules():
             m.set_processor(DenseProcessor())
@@ -260,12 +267,18 @@ class FluxTransformer(torch.nn.Module):
         temb = self.time_text_embed(timestep, guidance, pooled_projections)
         img = self.x_embedder(hidden_states)
         txt = self.context_embedder(encoder_hidden_states)
+        seq = self.sequence_parallel
+        gather = _same if seq is None else seq.gather
+        if seq is not None:  # this rank's token range of the image stream
+            img = seq.scatter(img)
         for b in self.transformer_blocks:
-            img, txt = b(img, txt, temb, rot, self.ops)
-        x = torch.cat([txt, img], dim=1)
+            img, txt = b(img, txt, temb, rot, self.ops, gather)
+        x = torch.cat([txt, gather(img)], dim=1)
+        if seq is not None:  # this rank's token range of the joined stream
+            x = seq.scatter(x)
         for b in self.single_transformer_blocks:
-            x = b(x, temb, rot, self.ops)
-        img = x[:, txt.shape[1]:]
+            x = b(x, temb, rot, self.ops, gather)
+        img = gather(x)[:, txt.shape[1]:]
         shift, scale = self.norm_out(F.silu(temb)).chunk(2, dim=-1)
         out = self.proj_out(_modulate(img, shift, scale))
         return FluxOutput(out) if return_dict else (out,)

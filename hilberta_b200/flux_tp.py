@@ -15,7 +15,15 @@ head-aligned so that every rank runs HilbertA attention on its own heads
 * replicated: embedders, adaLN modulation, norms, the output layer.
 
 A double-stream block all-reduces 4 times (attention and MLP outputs of the
-image and text streams), a single-stream block once.  The reference has no
+image and text streams), a single-stream block once.
+
+With ``sequence_parallel=True`` the image stream (double blocks) and the joined
+stream (single blocks) stay split by tokens between the layers: each rank keeps
+its contiguous token range, runs the adaLN modulation and gated residuals on it
+alone, all-gathers the modulated tokens before the column-parallel projections,
+and the row-parallel projections of those streams reduce-scatter (the same
+bytes as an all-reduce) instead of all-reducing.  The 512-token text stream of
+the double blocks stays replicated.  The reference has no
 multi-GPU step (it rejects diffusers' parallel attention,
 hilberta/flux_adapter.py:385); this is the head-parallel split of its
 attention (rank r owns heads [r*H/P, (r+1)*H/P)) carried through the block.
@@ -29,6 +37,43 @@ import torch.distributed as dist
 
 def _param(t):
     return torch.nn.Parameter(t.detach().contiguous(), requires_grad=False)
+
+
+class TokenShards:
+    """Token split of ``[B, S, C]`` streams over ``group``: rank r holds tokens
+    [r*S/P, (r+1)*S/P)."""
+
+    def __init__(self, group, world, rank):
+        self.group, self.world, self.rank = group, world, rank
+
+    def scatter(self, x):
+        S = x.shape[1]
+        if S % self.world:
+            raise ValueError(f"{S} tokens do not split over {self.world} ranks")
+        s = S // self.world
+        return x[:, self.rank * s:(self.rank + 1) * s].contiguous()
+
+    def gather(self, x):
+        B, s, C = x.shape
+        out = torch.empty(self.world * B, s, C, dtype=x.dtype, device=x.device)  # rank-major
+        dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        if B == 1:
+            return out.view(1, self.world * s, C)
+        return out.view(self.world, B, s, C).transpose(0, 1).reshape(B, self.world * s, C)
+
+    def reduce_scatter(self, y):
+        """Sum of ``y`` [B, S, C] over the ranks, this rank's token range."""
+        B, S, C = y.shape
+        if S % self.world:
+            raise ValueError(f"{S} tokens do not split over {self.world} ranks")
+        s = S // self.world
+        if B == 1:
+            src = y.reshape(self.world, s, C)
+        else:
+            src = y.view(B, self.world, s, C).transpose(0, 1).reshape(self.world * B, s, C)
+        out = torch.empty(B, s, C, dtype=y.dtype, device=y.device)
+        dist.reduce_scatter_tensor(out, src, group=self.group)
+        return out
 
 
 class _Overlap:
@@ -74,12 +119,13 @@ class RowParallelLinear(torch.nn.Module):
     this rank's input columns ``cols`` of the full layer; the bias enters once,
     through rank 0's GEMM."""
 
-    def __init__(self, full: torch.nn.Linear, cols: torch.Tensor, group, rank, overlap=None):
+    def __init__(self, full: torch.nn.Linear, cols: torch.Tensor, group, rank, overlap=None, shards=None):
         super().__init__()
         self.weight = _param(full.weight.index_select(1, cols.to(full.weight.device)))
         self.bias = _param(full.bias) if full.bias is not None and rank == 0 else None
         self.group = group
         self.overlap = overlap or _Overlap(1, None)
+        self.shards = shards  # TokenShards: reduce-scatter over tokens instead of all-reduce
 
     def forward(self, x):
         x2 = x.reshape(-1, x.shape[-1])
@@ -92,6 +138,9 @@ class RowParallelLinear(torch.nn.Module):
             else:
                 torch.addmm(self.bias, x2[s:e], wt, out=y[s:e])
 
+        if self.shards is not None:
+            gemm(0, y.shape[0])
+            return self.shards.reduce_scatter(y.view(*x.shape[:-1], -1))
         return self.overlap(y, gemm, self.group).view(*x.shape[:-1], -1)
 
 
@@ -99,7 +148,7 @@ class RowParallelJoined(torch.nn.Module):
     """Row-parallel form of ``flux_model.JoinedLinear``: this rank's attention
     columns ``cols_a`` and MLP columns ``cols_m``, partial sums all-reduced."""
 
-    def __init__(self, full, cols_a, cols_m, group, rank, overlap=None):
+    def __init__(self, full, cols_a, cols_m, group, rank, overlap=None, shards=None):
         super().__init__()
         w = full.weight
         self.weight_a = _param(w.index_select(1, cols_a.to(w.device)))
@@ -107,6 +156,7 @@ class RowParallelJoined(torch.nn.Module):
         self.bias = _param(full.bias) if full.bias is not None and rank == 0 else None
         self.group = group
         self.overlap = overlap or _Overlap(1, None)
+        self.shards = shards
 
     def forward(self, a, m, ops):
         a2, m2 = a.reshape(-1, a.shape[-1]), m.reshape(-1, m.shape[-1])
@@ -115,6 +165,9 @@ class RowParallelJoined(torch.nn.Module):
         def gemm(s, e):
             ops.joined_linear(a2[s:e], m2[s:e], self.weight_a, self.weight_m, self.bias, out=y[s:e])
 
+        if self.shards is not None:
+            gemm(0, y.shape[0])
+            return self.shards.reduce_scatter(y.view(*a.shape[:-1], -1))
         return self.overlap(y, gemm, self.group).view(*a.shape[:-1], -1)
 
 
@@ -136,15 +189,18 @@ def _slice(n, rank, world):
     return torch.arange(rank * s, (rank + 1) * s)
 
 
-def shard_flux_model(model, group=None, *, chunks=1, carveout=None, min_rows=2048):
+def shard_flux_model(model, group=None, *, chunks=1, carveout=None, min_rows=2048, sequence_parallel=False):
     """Split ``model`` (a ``FluxTransformer`` with identical weights on
     every rank) in place for this rank of ``group``; returns it.  Row-parallel
     layers over at least ``min_rows`` rows run as ``chunks`` row chunks whose
     all-reduces overlap the next chunk's GEMM, with ``carveout`` SMs kept free
-    of the GEMMs meanwhile (``chunks=1``: one GEMM, then one all-reduce)."""
+    of the GEMMs meanwhile (``chunks=1``: one GEMM, then one all-reduce).
+    ``sequence_parallel``: the image and joined streams split by tokens (see the
+    module docstring)."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     ov = _Overlap(chunks, carveout, min_rows)
+    sh = TokenShards(group, world, rank) if sequence_parallel else None
     first = (model.transformer_blocks or model.single_transformer_blocks)[0].attn
     heads = first.heads
     head_dim = first.to_q.weight.shape[0] // heads
@@ -155,13 +211,13 @@ def shard_flux_model(model, group=None, *, chunks=1, carveout=None, min_rows=204
         a = b.attn
         for name in ("to_q", "to_k", "to_v", "add_q_proj", "add_k_proj", "add_v_proj"):
             setattr(a, name, _column(getattr(a, name), head_cols))
-        a.to_out[0] = RowParallelLinear(a.to_out[0], head_cols, group, rank, ov)
+        a.to_out[0] = RowParallelLinear(a.to_out[0], head_cols, group, rank, ov, shards=sh)
         a.to_add_out = RowParallelLinear(a.to_add_out, head_cols, group, rank, ov)
         a.heads = heads // world
-        for ff in (b.ff_img, b.ff_txt):
+        for ff, stream_shards in ((b.ff_img, sh), (b.ff_txt, None)):
             hid = _slice(ff[0].weight.shape[0], rank, world)
             ff[0] = _column(ff[0], hid)
-            ff[1] = RowParallelLinear(ff[1], hid, group, rank, ov)
+            ff[1] = RowParallelLinear(ff[1], hid, group, rank, ov, shards=stream_shards)
     for b in model.single_transformer_blocks:
         a = b.attn
         for name in ("to_q", "to_k", "to_v"):
@@ -169,11 +225,12 @@ def shard_flux_model(model, group=None, *, chunks=1, carveout=None, min_rows=204
         a.heads = heads // world
         hid = _slice(b.proj_mlp.weight.shape[0], rank, world)
         b.proj_mlp = _column(b.proj_mlp, hid)
-        b.proj_out = RowParallelJoined(b.proj_out, head_cols, hid, group, rank, ov)
+        b.proj_out = RowParallelJoined(b.proj_out, head_cols, hid, group, rank, ov, shards=sh)
     model.tp_world, model.tp_rank = world, rank
+    model.sequence_parallel = sh
     if torch.cuda.is_available() and first.to_q.weight.is_cuda:
         torch.cuda.empty_cache()
     return model
 
 
-__all__ = ["RowParallelLinear", "RowParallelJoined", "shard_flux_model"]
+__all__ = ["RowParallelLinear", "RowParallelJoined", "TokenShards", "shard_flux_model"]

@@ -105,7 +105,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q, chunks=1):
+def _worker(rank, world, port, q, chunks=1, sp=False):
     try:
         from hilberta_b200.flux_tp import shard_flux_model
 
@@ -115,7 +115,7 @@ def _worker(rank, world, port, q, chunks=1):
         with torch.no_grad():
             full = model(**x).sample
             n_full = sum(p.numel() for p in model.parameters())
-            shard_flux_model(model, chunks=chunks, carveout=None, min_rows=1)
+            shard_flux_model(model, chunks=chunks, carveout=None, min_rows=1, sequence_parallel=sp)
             local = model(**x).sample
         n_local = sum(p.numel() for p in model.parameters())
         err = float((local - full).abs().max() / full.abs().max())
@@ -127,13 +127,15 @@ def _worker(rank, world, port, q, chunks=1):
         traceback.print_exc()
 
 
-@pytest.mark.parametrize("world,chunks", [(2, 1), (4, 1), (2, 3)])
-def test_tensor_parallel_step_matches_unsharded(world, chunks):
-    """chunks > 1: row-parallel GEMMs in row chunks with async all-reduces."""
+@pytest.mark.parametrize("world,chunks,sp", [(2, 1, False), (4, 1, False), (2, 3, False), (2, 1, True), (4, 1, True)])
+def test_tensor_parallel_step_matches_unsharded(world, chunks, sp):
+    """chunks > 1: row-parallel GEMMs in row chunks with async all-reduces;
+    sp: sequence parallelism (token-split streams, all-gather / reduce-scatter;
+    batch 2, so the batch-major reorder of both collectives is exercised)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, chunks)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, chunks, sp)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=180) for _ in procs)

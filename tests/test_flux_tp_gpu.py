@@ -24,7 +24,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, sp):
     try:
         import hilberta_b200 as hb
         from hilberta_b200.flux_model import FluxTransformer, step_inputs
@@ -40,7 +40,7 @@ def _worker(rank, world, port, q):
         x = step_inputs(32, plan.text_tokens, dev, seed=3, text_dim=64, pooled_dim=32)
         with torch.inference_mode(), hb.persistent_flux_attention(model, plan, backend="paired"):
             full = model(**x).sample.float()
-        shard_flux_model(model)
+        shard_flux_model(model, sequence_parallel=sp)
         with torch.inference_mode(), hb.persistent_flux_attention(model, plan, backend="paired"):
             local = model(**x).sample.float()
         rel = float((local - full).norm() / full.norm())
@@ -55,11 +55,13 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tensor_parallel_hilberta_step_two_gpus():
+@pytest.mark.parametrize("sp", [False, True])
+def test_tensor_parallel_hilberta_step_two_gpus(sp):
+    """sp: image / joined streams split by tokens (all-gather, reduce-scatter)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, sp)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=240) for _ in procs)
