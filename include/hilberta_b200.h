@@ -24,6 +24,10 @@
  *                                  reorder passes of hilberta/sampling_layout.py:88-116
  *   hb_paired_fwd_allgather        the same kernel fused with the head-output gather
  *                                  before to_out (hilberta/flux_adapter.py:328-339)
+ *   hb_expand_kv128                KV128 paired metadata (hilberta/paired_metadata.py:26-51,
+ *                                  key_block_size=128) as the equivalent KV64 table
+ *   hb_adaln_residual              the adaLN-Zero modulation / gated residual of the FLUX
+ *                                  blocks around the processor of flux_adapter.py:259-340
  */
 #ifndef HILBERTA_B200_H
 #define HILBERTA_B200_H
