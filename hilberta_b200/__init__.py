@@ -29,7 +29,7 @@ from .prep import norm_rope_pack, prepare_qkv
 from .processor import HilbertAProcessor
 from .flux_adapter import persistent_flux_attention
 from .sampling_layout import sample_flux_persistent
-from .sparse_kernel import explicit_mask, validate_metadata
+from .sparse_kernel import explicit_mask, sparse_attention, validate_metadata
 
 __version__ = "0.1.0"
 
@@ -45,6 +45,7 @@ __all__ = [
     "validate_metadata",
     "explicit_mask",
     "paired_attention",
+    "sparse_attention",
     "device_status",
     "RasterOrder",
     "raster_order",

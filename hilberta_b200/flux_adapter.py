@@ -20,10 +20,11 @@ Inside the context:
   (flux_adapter.py:149-256);
 * every attention module runs layer ``i``'s processor on phase ``i % 4``
   (flux_adapter.py:259-340): ``"paired"`` = ``HilbertAProcessor`` (fused Q/K/V
-  preparation + the sm_100a paired kernel); ``"sparse"`` = the same kernel (the
-  reference's unpaired kernel computes the same masked attention from the same
-  rows); ``"sdpa_reference"`` = the correctness path, torch ops restating
-  diffusers' RMSNorm and rotary embedding and SDPA under the plan's dense mask.
+  preparation + the sm_100a paired kernel on the phase's paired rows);
+  ``"sparse"`` = the same preparation and ``sparse_attention`` on the phase's
+  unpaired rows (which pairs them once and runs the same kernel);
+  ``"sdpa_reference"`` = the correctness path, torch ops restating diffusers'
+  RMSNorm and rotary embedding and SDPA under the plan's dense mask.
 """
 
 from __future__ import annotations
@@ -37,6 +38,7 @@ from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from .plan_bank import PlanBank
 from .processor import HilbertAProcessor
+from .sparse_kernel import sparse_attention
 
 _ACTIVE = "_flux_kernel_persistent_layout"
 _SDP_BACKENDS = {"math": SDPBackend.MATH, "efficient": SDPBackend.EFFICIENT_ATTENTION}
@@ -130,13 +132,25 @@ def _rotary(x, cos, sin):
     return (x.float() * cos[None, :, None] + rot.float() * sin[None, :, None]).to(x.dtype)
 
 
+class _SparseRowsProcessor(HilbertAProcessor):
+    """``HilbertAProcessor`` whose attention is ``sparse_attention`` on the
+    phase's unpaired rows, as the reference's "sparse" backend calls it
+    (flux_adapter.py:313-326)."""
+
+    def _attend(self, q, k, v):
+        ids, counts = self.bank.on_device(q.device)["phases"][self.phase]
+        return sparse_attention(q, k, v, ids, counts, global_tokens=self.bank.global_tokens,
+                                block_size=self.bank.block_size, **self.kernel_options)
+
+
 class PersistentFluxProcessor:
     """Layer ``layer``'s processor inside ``persistent_flux_attention``."""
 
     def __init__(self, runtime, layer, backend, kernel_options):
         self.runtime, self.layer, self.phase = runtime, int(layer), int(layer) % 4
         self.backend, self.kernel_options = backend, dict(kernel_options)
-        self.native = HilbertAProcessor(runtime.bank, layer, kernel_options) if backend != "sdpa_reference" else None
+        native = {"paired": HilbertAProcessor, "sparse": _SparseRowsProcessor}.get(backend)
+        self.native = native(runtime.bank, layer, kernel_options) if native is not None else None
 
     def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, image_rotary_emb=None):
         if not self.runtime.in_forward:

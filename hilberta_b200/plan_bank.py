@@ -67,9 +67,7 @@ class PlanBank:
         for ids, counts in self.phases:
             self._check_rows(ids, counts, dev)
         self.paired_phases = None
-        # "sparse" (the reference's unpaired kernel over the same rows) runs the
-        # paired kernel here: the same masked attention
-        if self.info["backend"] in ("paired", "sparse"):
+        if self.info["backend"] == "paired":
             if self.block_size != 64:
                 raise ValueError("Paired backend requires 64-token physical blocks")
             self.paired_phases = [

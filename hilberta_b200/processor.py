@@ -76,9 +76,12 @@ class HilbertAProcessor:
         q, k, v = (x.transpose(1, 2) for x in packed)  # [B, H, S, D] views of [B, S, H, D]
         if q.shape[2] != self.bank.total_tokens:
             raise ValueError("Native attention sequence length does not match the plan")
+        return self._attend(q, k, v).transpose(1, 2).flatten(2, 3)
+
+    def _attend(self, q, k, v):
+        """The attention of the layer's phase on the prepared [B, H, S, D] views."""
         metadata = self.bank.on_device(q.device)["paired_phases"][self.phase]
-        result = paired_attention(q, k, v, metadata, **self.kernel_options)
-        return result.transpose(1, 2).flatten(2, 3)
+        return paired_attention(q, k, v, metadata, **self.kernel_options)
 
     def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, image_rotary_emb=None):
         if attention_mask is not None:
