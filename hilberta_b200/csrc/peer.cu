@@ -60,3 +60,10 @@ extern "C" int hb_ipc_close(void* ptr, uint64_t offset) {
     HB_CUDA_TRY(cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset));
     return HB_OK;
 }
+
+extern "C" int hb_peer_copy(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!dst || !src) return HB_ERR_ARG;
+    if (bytes == 0) return HB_OK;
+    HB_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+    return HB_OK;
+}

@@ -92,10 +92,13 @@ class PeerAllGather:
     head slice ``[B, heads/P, N, D]`` and returns the full ``[B, heads, N, D]``
     output (a view of storage in ``layout`` order: "bhnd", or "bnhd" as the
     processor's hidden states before ``flatten(2, 3)``), complete on return of
-    the launch on the current stream.  Outputs alternate between two buffers, so
-    a returned tensor stays valid until the call after next.  After a call that
-    reports ``HB_DEV_PEER_TIMEOUT`` (``device_status``) the ranks' flags may
-    disagree: close the instance and build a new one.
+    the launch on the current stream.  Outputs alternate between two buffers.
+    A returned tensor is valid for work that is ordered on the stream before
+    this rank's next call: a peer may start writing the same buffer in its call
+    after next as soon as this rank's next call has finished, so read or copy
+    the output (or queue the work that consumes it) before making the next call.
+    After a call that reports ``HB_DEV_PEER_TIMEOUT`` (``device_status``) the
+    ranks' flags may disagree: close the instance and build a new one.
     """
 
     def __init__(self, batch, heads, tokens, head_dim, *, dtype=torch.bfloat16, layout="bhnd", group=None,
@@ -164,6 +167,40 @@ class PeerAllGather:
             peers.flags[r] = self._ptrs[r][2]
         _launch_allgather(q, k, v, full, metadata, N_, G, scale, peers)
         return full
+
+    def measure_link_gbs(self, reps=3):
+        """Collective, between calls only: every rank copies the bytes one call
+        sends to each peer (its own head rows) into every peer's buffer with
+        plain copy-engine transfers (``hb_peer_copy``, one stream per peer), all
+        ranks at once, as the fused call's stores load the links.  Returns this
+        rank's send bandwidth in GB/s (bytes sent over device time, best of
+        `reps`).  It overwrites the buffers' contents."""
+        if self._ptrs is None:
+            raise RuntimeError("PeerAllGather is closed")
+        B, H, N, D = self.shape
+        nbytes = B * (self.head1 - self.head0) * N * D * self._bufs[0].element_size()
+        src = self._ptrs[self.rank][1] + self.rank * nbytes  # this rank's region of its idle second buffer
+        lib = _lib.lib()
+        main = torch.cuda.current_stream(self.device)
+        side = [torch.cuda.Stream(self.device) for _ in range(self.world - 1)]
+        best = float("inf")
+        for _ in range(reps):
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(main)
+            peers = [r for r in range(self.world) if r != self.rank]
+            for s, r in zip(side, peers):
+                s.wait_event(e0)
+                _lib.check(lib.hb_peer_copy(ctypes.c_void_p(self._ptrs[r][0] + self.rank * nbytes),
+                                            ctypes.c_void_p(src), nbytes, ctypes.c_void_p(s.cuda_stream)),
+                           "hb_peer_copy")
+                main.wait_stream(s)
+            e1.record(main)
+            torch.cuda.synchronize(self.device)
+            best = min(best, e0.elapsed_time(e1))
+        dist.barrier(group=self.group)
+        return (self.world - 1) * nbytes / (best * 1e-3) / 1e9
 
     def close(self):
         """Unmap the peers' buffers once every rank is done with every call (collective)."""

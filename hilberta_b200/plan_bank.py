@@ -103,19 +103,26 @@ class PlanBank:
     def on_device(self, device):
         key = str(device)
         if key not in self.device_cache:
-            entry = {
-                "order": self.order.to(device),
-                "inverse": self.inverse.to(device),
-                "phases": [(ids.to(device), counts.to(device)) for ids, counts in self.phases],
-            }
-            if self.paired_phases is not None:
-                entry["paired_phases"] = [p.to(device) for p in self.paired_phases]
-            if self._raster is not None:
-                r = self._raster
-                entry["raster"] = type(r)(r.text_tokens, r.grid, r.block_origin.to(device))
-            self.device_cache[key] = entry
+            # Normal tensors even when the first call runs under inference mode:
+            # the caches keyed on a table's version counter (the sparse
+            # backend's pairing, the KV128 expansion) skip inference tensors.
+            with torch.inference_mode(False):
+                self.device_cache[key] = self._device_entry(device)
             self.info["metadata_device_copies"] = len(self.device_cache)
         return self.device_cache[key]
+
+    def _device_entry(self, device):
+        entry = {
+            "order": self.order.to(device, copy=True),
+            "inverse": self.inverse.to(device, copy=True),
+            "phases": [(ids.to(device, copy=True), counts.to(device, copy=True)) for ids, counts in self.phases],
+        }
+        if self.paired_phases is not None:
+            entry["paired_phases"] = [p.to(device) for p in self.paired_phases]
+        if self._raster is not None:
+            r = self._raster
+            entry["raster"] = type(r)(r.text_tokens, r.grid, r.block_origin.to(device, copy=True))
+        return entry
 
     def dense_mask(self, phase, device):
         """Dense [N, N] boolean mask of a phase (correctness reference only),

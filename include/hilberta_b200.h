@@ -243,6 +243,12 @@ int hb_paired_fwd_allgather(const void* q, const void* k, const void* v, const i
 int hb_ipc_export(const void* ptr, void* handle, uint64_t* offset);
 int hb_ipc_open(const void* handle, uint64_t offset, void** ptr);
 int hb_ipc_close(void* ptr, uint64_t offset);
+/* One plain device-to-device copy of `bytes` (cudaMemcpyAsync on `stream`);
+ * `dst` may be a mapping from hb_ipc_open.  No counterpart in the reference
+ * (it has no multi-GPU path): the copy-engine transfer into a peer's memory
+ * that callers time to know the NVLink bandwidth the fused all-gather's peer
+ * stores are held against. */
+int hb_peer_copy(void* dst, const void* src, size_t bytes, void* stream);
 
 /* ---- Q/K/V preparation before the attention ----------------------------- */
 /* The FLUX processor's steps between the projections and the attention
@@ -319,9 +325,10 @@ int hb_adaln_residual(const void* x, int64_t x_rs, const void* y, int64_t y_rs, 
  * the GPU (different streams, no ordering between them) race; serialise them
  * or use hb_paired_fwd with separate workspaces.  Device status bits are not
  * reported by this variant.  Problems needing more than HB_NOALLOC_MAX_ITEMS
- * work items (B*H*N/128) are rejected with HB_ERR_UNSUPPORTED. */
+ * (2^30 - 1) work items (B*H*N/128) are rejected with HB_ERR_UNSUPPORTED before
+ * any CUDA call; that is the same bound the kernel's scheduler has. */
 #define HB_NOALLOC_SCRATCH_BYTES 256
-#define HB_NOALLOC_MAX_ITEMS (1 << 30)
+#define HB_NOALLOC_MAX_ITEMS ((1 << 30) - 1)
 int hb_paired_fwd_noalloc(const void* q, const void* k, const void* v, void* out,
                           const int64_t* strides, int B, int H, int N, int D, int G, int W,
                           int key_block_size, const int32_t* kv_indices, const int32_t* kv_flags,

@@ -34,3 +34,37 @@ def test_sparse_attention_equals_paired_and_oracle():
     ref = ao.masked_attention_fp32(q.cpu(), k.cpu(), v.cpu(), ao.block_mask_from_rows(p.kv_indices, p.kv_counts, N, G))
     err = (out.float().cpu() - ref).abs()
     assert float(err.max()) <= 2e-2 and float(err.mean()) <= 2e-3
+
+
+def test_sparse_backend_under_inference_mode_pairs_each_table_once(monkeypatch):
+    """The adapter's sparse backend reads the unpaired rows from PlanBank's
+    device copies.  Built on a first call under inference mode they must still
+    be normal tensors (inference tensors carry no version counter), so the
+    pairing cache hits and every phase is paired once, not on every call."""
+    import hilberta_b200 as hb
+    from hilberta_b200 import paired_metadata as pm
+    from hilberta_b200 import sparse_kernel as sk
+
+    calls = []
+    real = pm.pair_metadata
+
+    def counting(*a, **kw):
+        calls.append(1)
+        return real(*a, **kw)
+
+    monkeypatch.setattr(pm, "pair_metadata", counting)
+    plan = hb.bridge_k_plan(4, 1, False, grid_size=32)
+    N, G = plan.total_tokens, plan.global_tokens
+    bank = hb.PlanBank(plan, backend="sparse")
+    q, k, v = (x.cuda() for x in ao.seeded_qkv(1, 2, N, 128, seed=42))
+    sk._paired_rows_cache.clear()
+    outs = []
+    with torch.inference_mode():
+        for layer in range(12):  # three passes over the four phases
+            ids, counts = bank.on_device(q.device)["phases"][layer % 4]
+            assert not ids.is_inference() and not counts.is_inference()
+            outs.append(sk.sparse_attention(q, k, v, ids, counts, global_tokens=G))
+    assert len(calls) == 4
+    for layer in range(4, 12):
+        assert torch.equal(outs[layer], outs[layer % 4])
+    assert hb.device_status() == 0

@@ -17,8 +17,6 @@ import ctypes
 import pytest
 import torch
 
-pytestmark = pytest.mark.gpu
-
 MAX_ABS = 2e-2
 MEAN_ABS = 2e-3
 
@@ -27,6 +25,7 @@ def _strides(q, k, v, out):
     return (ctypes.c_int64 * 12)(*q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *out.stride()[:3])
 
 
+@pytest.mark.gpu
 def test_noalloc_matches_allocating_entry_on_two_calls():
     import hilberta_b200 as hb
     from hilberta_b200 import _lib
@@ -65,13 +64,19 @@ def test_noalloc_matches_allocating_entry_on_two_calls():
         assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS, (call, float(err.max()))
 
 
-def test_noalloc_rejects_problems_beyond_its_limit():
+@pytest.mark.parametrize("items_log2", [30, 31])
+def test_noalloc_rejects_problems_beyond_its_limit(items_log2):
+    """HB_NOALLOC_MAX_ITEMS is 2^30 - 1, the scheduler's own bound: exactly 2^30
+    work items (B*H*N/128) is already refused, before any CUDA call, so this
+    needs no GPU and the fake pointers are never touched."""
     from hilberta_b200 import _lib
 
     lib = _lib.lib()
     fake = ctypes.c_void_p(1 << 20)
     strides = (ctypes.c_int64 * 12)(*([1] * 12))
-    # B*H*N/128 = 2^31 work items > HB_NOALLOC_MAX_ITEMS (2^30)
-    rc = lib.hb_paired_fwd_noalloc(fake, fake, fake, fake, strides, 1 << 10, 1 << 10, 1 << 18, 128, 0, 1, 64,
+    B, H = 1 << 10, 1 << 10
+    N = 128 << (items_log2 - 20)
+    assert B * H * (N // 128) == 1 << items_log2
+    rc = lib.hb_paired_fwd_noalloc(fake, fake, fake, fake, strides, B, H, N, 128, 0, 1, 64,
                                    fake, fake, fake, 0.1, 1, None)
     assert rc == _lib.HB_ERR_UNSUPPORTED
