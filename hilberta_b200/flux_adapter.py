@@ -1,36 +1,49 @@
 """Transformer-scope adapter: run a FLUX transformer in a plan's persistent
 token layout with HilbertA attention in every joint-attention call.
 
-``persistent_flux_attention(model, plan, backend=...)`` is the reference
-adapter's entry (hilberta/flux_adapter.py:343-430): the same arguments, checks,
-messages and ``info`` counters, for any model with the module names and forward
-signature of diffusers' ``FluxTransformer2DModel`` (``transformer_blocks``,
-``single_transformer_blocks``, ``attn.set_processor``, ``forward(hidden_states,
-encoder_hidden_states, ..., img_ids, txt_ids, ...)``).  Nothing here imports
-diffusers: the reference's type checks on the installed processors become checks
-of their attributes (no parallel config, native attention backend).
+``persistent_flux_attention(model, plan, backend=...)`` keeps the reference
+adapter's contract (hilberta/flux_adapter.py:149-256 and 343-440): its
+arguments, the exception types and messages of its refusals, and the keys and
+meaning of the ``info`` dict it yields.  It serves any model with the module
+names and forward signature of diffusers' ``FluxTransformer2DModel``
+(``transformer_blocks``, ``single_transformer_blocks``, ``attn.set_processor``,
+``forward(hidden_states, encoder_hidden_states, ..., img_ids, txt_ids, ...)``).
+Nothing here imports diffusers: the reference's type checks on the installed
+processors become checks of their attributes (no parallel config, the native
+attention backend).
 
-Inside the context:
+How it is built:
 
-* a forward pre-hook checks the call (inference only, token counts, no
-  ControlNet residuals, only a LoRA ``scale`` in ``joint_attention_kwargs``) and,
-  with ``layout_scope="transformer"``, gathers ``hidden_states`` and ``img_ids``
-  into the plan's physical order once; a post-hook (which also runs when the
-  forward raises) gathers the prediction back to raster order
-  (flux_adapter.py:149-256);
-* every attention module runs layer ``i``'s processor on phase ``i % 4``
-  (flux_adapter.py:259-340): ``"paired"`` = ``HilbertAProcessor`` (fused Q/K/V
-  preparation + the sm_100a paired kernel on the phase's paired rows);
-  ``"sparse"`` = the same preparation and ``sparse_attention`` on the phase's
-  unpaired rows (which pairs them once and runs the same kernel);
-  ``"sdpa_reference"`` = the correctness path, torch ops restating diffusers'
-  RMSNorm and rotary embedding and SDPA under the plan's dense mask.
+* refusals are data: ``_Refusal`` rows (a test, an exception type, the
+  message), checked in order by ``_refuse`` on the arguments, the model, each
+  attention block and each transformer call;
+* ``_Boundary`` owns the model-level hooks.  Its entry hook binds the call to
+  the forward signature, applies the call refusals and hands ``hidden_states`` /
+  ``img_ids`` to the scope; its exit hook (registered first, and run even when
+  the forward raises) hands the prediction back to the scope;
+* the scope is a strategy object: ``_GatherAtBoundary`` (``layout_scope=
+  "transformer"``: one gather into the plan's order on entry and one back on
+  exit per call) or ``_AlreadyPacked`` (``"sampling"``: the tokens stay packed
+  for the whole trajectory, see ``sampling_layout``);
+* everything the context changes is undone by an ``ExitStack`` in reverse
+  order of installation: hooks, processors, the plan's device copies, the
+  model's marker.
+
+Every attention module runs layer ``i``'s processor on tile phase ``i % 4``
+(flux_adapter.py:259-340): ``"paired"`` = ``HilbertAProcessor`` (fused Q/K/V
+preparation and the sm_100a paired kernel on the phase's paired rows);
+``"sparse"`` = the same preparation and ``sparse_attention`` on the phase's
+unpaired rows (paired once per table, same kernel); ``"sdpa_reference"`` = the
+correctness path, torch ops restating diffusers' RMSNorm and rotary embedding
+and SDPA under the plan's dense mask.
 """
 
 from __future__ import annotations
 
 import contextlib
 import inspect
+from dataclasses import dataclass
+from typing import Any, Callable
 
 import torch
 import torch.nn.functional as F
@@ -40,76 +53,162 @@ from .plan_bank import PlanBank
 from .processor import HilbertAProcessor
 from .sparse_kernel import sparse_attention
 
+# Markers set on a model by this context and by the reference's image-mask
+# context (nesting either one inside the other is refused).
 _ACTIVE = "_flux_kernel_persistent_layout"
+_MASK_CONTEXT = "_hilbert_flux_mask_context_active"
 _SDP_BACKENDS = {"math": SDPBackend.MATH, "efficient": SDPBackend.EFFICIENT_ATTENTION}
+_BACKENDS = ("sdpa_reference", "sparse", "paired")
 
 
-class _Runtime:
-    """Call state of one context: the plan bank, the model's forward signature,
-    whether a transformer call is in progress."""
+@dataclass(frozen=True)
+class _Refusal:
+    applies: Callable[[Any], bool]
+    error: type
+    message: str
 
-    def __init__(self, model, bank, info):
+
+def _refuse(refusals, subject):
+    """Raise the first refusal whose test holds for `subject`."""
+    for r in refusals:
+        if r.applies(subject):
+            raise r.error(r.message)
+
+
+def _tensor_with(x, ndims, tail):
+    """x is a tensor of one of `ndims` ranks whose trailing shape is `tail`."""
+    return isinstance(x, torch.Tensor) and x.ndim in ndims and tuple(x.shape[-len(tail):]) == tuple(tail)
+
+
+_ARGUMENT_REFUSALS = (
+    _Refusal(lambda a: a["layout_scope"] not in ("transformer", "sampling"), ValueError,
+             "layout_scope must be transformer or sampling"),
+    _Refusal(lambda a: a["backend"] not in _BACKENDS or a["sdpa_backend"] not in _SDP_BACKENDS, ValueError,
+             "backend must be sdpa_reference/sparse/paired; sdpa_backend must be math/efficient"),
+)
+
+_MODEL_REFUSALS = (
+    _Refusal(lambda m: getattr(m, _ACTIVE, False) or getattr(m, _MASK_CONTEXT, False), RuntimeError,
+             "Nested/conflicting Flux layout or image-mask contexts are unsupported"),
+    _Refusal(lambda m: m.training or getattr(m, "gradient_checkpointing", False), ValueError,
+             "Native Flux model must be in eval mode without gradient checkpointing"),
+    _Refusal(lambda m: getattr(m, "_cache_config", None) is not None, ValueError,
+             "Transformer cache state needs a separate layout-aware implementation"),
+    _Refusal(lambda m: len(m.transformer_blocks) == 0 or len(m.single_transformer_blocks) == 0, ValueError,
+             "Both native Flux joint and single blocks are required"),
+)
+
+# subject: (block, is_joint)
+_BLOCK_REFUSALS = (
+    _Refusal(lambda b: isinstance(b[0].attn.processor, PersistentFluxProcessor)
+             or getattr(b[0].attn.processor, "_attention_backend", None) not in (None, "native")
+             or getattr(b[0].attn.processor, "_parallel_config", None) is not None, ValueError,
+             "Only native, non-parallel Diffusers FluxAttnProcessor is supported"),
+    _Refusal(lambda b: (b[0].attn.added_kv_proj_dim is not None) != b[1], ValueError,
+             "Native joint/single projection types disagree with block layout"),
+)
+
+# subject: (arguments of the bound forward call, plan bank)
+_CALL_REFUSALS = (
+    _Refusal(lambda c: not (isinstance(c[0].get("hidden_states"), torch.Tensor) and c[0]["hidden_states"].ndim == 3
+                            and c[0]["hidden_states"].shape[1] == c[1].image_tokens), ValueError,
+             "hidden_states image-token count does not match the plan"),
+    _Refusal(lambda c: not (isinstance(c[0].get("encoder_hidden_states"), torch.Tensor)
+                            and c[0]["encoder_hidden_states"].ndim == 3
+                            and c[0]["encoder_hidden_states"].shape[:2] == (c[0]["hidden_states"].shape[0],
+                                                                            c[1].text_tokens)), ValueError,
+             "encoder_hidden_states batch/text-token count does not match the plan"),
+    _Refusal(lambda c: not _tensor_with(c[0].get("img_ids"), (2, 3), (c[1].image_tokens, 3)), ValueError,
+             "img_ids must match image token identities with final shape [image_tokens,3]"),
+    _Refusal(lambda c: not _tensor_with(c[0].get("txt_ids"), (2, 3), (c[1].text_tokens, 3)), ValueError,
+             "txt_ids must match the native text prefix"),
+    _Refusal(lambda c: c[0].get("controlnet_block_samples") is not None
+             or c[0].get("controlnet_single_block_samples") is not None, ValueError,
+             "ControlNet residuals require a separate layout-aware implementation"),
+    _Refusal(lambda c: c[0].get("joint_attention_kwargs") is not None
+             and (not isinstance(c[0]["joint_attention_kwargs"], dict) or set(c[0]["joint_attention_kwargs"]) - {"scale"}),
+             ValueError, "Only native scalar LoRA scale is supported in joint_attention_kwargs; no IP-adapter/extra masks"),
+)
+
+
+class _GatherAtBoundary:
+    """layout_scope="transformer": raster tensors at the model's boundary; the
+    image tokens (and their position ids) are gathered into the plan's order
+    when a call enters and the prediction is gathered back when it leaves."""
+
+    def __init__(self, bank, info):
         self.bank, self.info = bank, info
-        self.signature = inspect.signature(model.forward)
-        self.in_forward = False
-        self.expected_output_batch = None
 
-    def before(self, model, args, kwargs):
+    def _gather(self, x, dim, which):
+        self.info["image_layout_gather_read_write_bytes"] += 2 * x.numel() * x.element_size()
+        return x.index_select(dim, self.bank.on_device(x.device)[which])
+
+    def enter(self, arguments):
+        hidden, ids = arguments["hidden_states"], arguments["img_ids"]
+        ids_moved = ids.index_select(ids.ndim - 2, self.bank.on_device(ids.device)["order"])
+        arguments["hidden_states"] = self._gather(hidden, 1, "order")
+        arguments["img_ids"] = ids_moved
+        self.info["image_reorder_calls"] += 1
+        self.info["image_id_reorder_calls"] += 1
+
+    def leave(self, prediction):
+        self.info["image_inverse_calls"] += 1
+        return self._gather(prediction, 1, "inverse")
+
+
+class _AlreadyPacked:
+    """layout_scope="sampling": the caller keeps the tokens in the plan's order
+    for the whole trajectory; nothing moves at the model's boundary."""
+
+    def enter(self, arguments):
+        pass
+
+    def leave(self, prediction):
+        return prediction
+
+
+def _split_prediction(output):
+    """(prediction tensor, function rebuilding the output around a new one) of a
+    transformer output: an object with ``sample`` or a one-element tuple."""
+    if hasattr(output, "sample"):
+        return output.sample, lambda t: type(output)(sample=t)
+    if isinstance(output, tuple) and len(output) == 1:
+        return output[0], lambda t: (t,)
+    raise TypeError("Expected native Flux Transformer2DModelOutput or one-element tuple")
+
+
+class _Boundary:
+    """The model-level hooks of one context.  ``in_forward`` is true between a
+    call's entry and exit hooks; the processors refuse to run outside it."""
+
+    def __init__(self, model, bank, info, scope):
+        self.bank, self.info, self.scope = bank, info, scope
+        self._bind = inspect.signature(model.forward).bind
+        self.in_forward = False
+        self._batch = None
+
+    def on_entry(self, module, args, kwargs):
         if self.in_forward:
             raise RuntimeError("Reentrant Transformer forwards are unsupported in persistent-layout context")
         if torch.is_grad_enabled():
             raise RuntimeError("Persistent sparse Flux is inference-only; use torch.no_grad or inference_mode")
-        bound = self.signature.bind(*args, **kwargs)
-        values = bound.arguments
-        hidden, text = values.get("hidden_states"), values.get("encoder_hidden_states")
-        ids, text_ids = values.get("img_ids"), values.get("txt_ids")
-        bank = self.bank
-        if not isinstance(hidden, torch.Tensor) or hidden.ndim != 3 or hidden.shape[1] != bank.image_tokens:
-            raise ValueError("hidden_states image-token count does not match the plan")
-        if not isinstance(text, torch.Tensor) or text.ndim != 3 or text.shape[:2] != (hidden.shape[0], bank.text_tokens):
-            raise ValueError("encoder_hidden_states batch/text-token count does not match the plan")
-        if not isinstance(ids, torch.Tensor) or ids.ndim not in (2, 3) or ids.shape[-2:] != (bank.image_tokens, 3):
-            raise ValueError("img_ids must match image token identities with final shape [image_tokens,3]")
-        if (not isinstance(text_ids, torch.Tensor) or text_ids.ndim not in (2, 3)
-                or text_ids.shape[-2:] != (bank.text_tokens, 3)):
-            raise ValueError("txt_ids must match the native text prefix")
-        if values.get("controlnet_block_samples") is not None or values.get("controlnet_single_block_samples") is not None:
-            raise ValueError("ControlNet residuals require a separate layout-aware implementation")
-        extra = values.get("joint_attention_kwargs")
-        if extra is not None and (not isinstance(extra, dict) or set(extra) - {"scale"}):
-            raise ValueError(
-                "Only native scalar LoRA scale is supported in joint_attention_kwargs; no IP-adapter/extra masks")
-        if self.info["layout_scope"] == "transformer":
-            values["hidden_states"] = hidden.index_select(1, bank.on_device(hidden.device)["order"])
-            values["img_ids"] = ids.index_select(ids.ndim - 2, bank.on_device(ids.device)["order"])
-            self.info["image_reorder_calls"] += 1
-            self.info["image_id_reorder_calls"] += 1
-            self.info["image_layout_gather_read_write_bytes"] += 2 * hidden.numel() * hidden.element_size()
-        self.expected_output_batch = hidden.shape[0]
+        call = self._bind(*args, **kwargs)
+        _refuse(_CALL_REFUSALS, (call.arguments, self.bank))
+        self._batch = call.arguments["hidden_states"].shape[0]
+        self.scope.enter(call.arguments)
         self.in_forward = True
         self.info["transformer_calls"] += 1
-        return bound.args, bound.kwargs
+        return call.args, call.kwargs
 
-    def after(self, model, args, output):
-        # registered with always_call: a forward that raised still clears the
-        # call state here (and has no prediction to restore)
-        active, self.in_forward = self.in_forward, False
-        if output is None or not active:
+    def on_exit(self, module, args, output):
+        was_running, self.in_forward = self.in_forward, False  # also after a forward that raised
+        if output is None or not was_running:
             return output
-        if hasattr(output, "sample"):
-            value = output.sample
-        elif isinstance(output, tuple) and len(output) == 1:
-            value = output[0]
-        else:
-            raise TypeError("Expected native Flux Transformer2DModelOutput or one-element tuple")
-        if value.ndim != 3 or value.shape[:2] != (self.expected_output_batch, self.bank.image_tokens):
+        prediction, rebuild = _split_prediction(output)
+        if prediction.ndim != 3 or tuple(prediction.shape[:2]) != (self._batch, self.bank.image_tokens):
             raise ValueError("Transformer output shape does not match image layout")
-        if self.info["layout_scope"] == "sampling":
-            return output
-        restored = value.index_select(1, self.bank.on_device(value.device)["inverse"])
-        self.info["image_inverse_calls"] += 1
-        self.info["image_layout_gather_read_write_bytes"] += 2 * value.numel() * value.element_size()
-        return type(output)(sample=restored) if hasattr(output, "sample") else (restored,)
+        moved = self.scope.leave(prediction)
+        return output if moved is prediction else rebuild(moved)
 
 
 def _rms_norm(x, norm):
@@ -191,80 +290,62 @@ class PersistentFluxProcessor:
         return attn.to_out[1](attn.to_out[0](image)), attn.to_add_out(text)
 
 
+def _info(backend, sdpa_backend, kernel_options, layout_scope, joint, single):
+    """The ``info`` dict the context yields: its settings, then counters the
+    hooks, processors and plan bank advance."""
+    layers = joint + single
+    boundary = "one Transformer-entry/exit gather" if layout_scope == "transformer" else "packed throughout sampling"
+    settings = dict(backend=backend, sdpa_backend=sdpa_backend, kernel_options=dict(kernel_options),
+                    layout_scope=layout_scope)
+    counters = dict.fromkeys(("transformer_calls", "image_reorder_calls", "image_inverse_calls",
+                              "image_id_reorder_calls", "per_layer_image_permutations", "metadata_device_copies",
+                              "reference_masks_prepared", "image_layout_gather_read_write_bytes"), 0)
+    layout = dict(layer_calls=[0] * layers, layer_phases=[i % 4 for i in range(layers)], joint_layers=joint,
+                  single_layers=single, layout="native text prefix; shared image prefix; remaining image tokens; "
+                  + boundary)
+    guarantees = dict(shared_tokens_keep_image_projections=True, native_dynamic_text_preserved=True,
+                      precision="unchanged; native QK RMSNorm and RoPE", weights_modified=False,
+                      kernel="torch SDPA, dense plan mask" if backend == "sdpa_reference"
+                      else "sm_100a paired (hb_paired_fwd)")
+    return {**settings, **counters, **layout, **guarantees}
+
+
 @contextlib.contextmanager
 def persistent_flux_attention(model, plan, backend="sdpa_reference", sdpa_backend="math", kernel_options=None, *,
                               layout_scope="transformer"):
-    """Reversibly run a FLUX transformer in the plan's persistent layout
-    (flux_adapter.py:343-430): processors installed on entry and restored on
-    exit, plan metadata moved once per device, yields the ``info`` dict."""
-    if layout_scope not in ("transformer", "sampling"):
-        raise ValueError("layout_scope must be transformer or sampling")
-    if backend not in ("sdpa_reference", "sparse", "paired") or sdpa_backend not in _SDP_BACKENDS:
-        raise ValueError("backend must be sdpa_reference/sparse/paired; sdpa_backend must be math/efficient")
-    if getattr(model, _ACTIVE, False) or getattr(model, "_hilbert_flux_mask_context_active", False):
-        raise RuntimeError("Nested/conflicting Flux layout or image-mask contexts are unsupported")
-    if model.training or getattr(model, "gradient_checkpointing", False):
-        raise ValueError("Native Flux model must be in eval mode without gradient checkpointing")
-    if getattr(model, "_cache_config", None) is not None:
-        raise ValueError("Transformer cache state needs a separate layout-aware implementation")
+    """Reversibly run a FLUX transformer in the plan's persistent layout:
+    processors installed on entry and restored on exit, plan metadata checked
+    once and copied once per device, the ``info`` dict yielded.  Single-
+    threaded; reentrant forwards, ControlNet residuals and IP-adapter inputs are
+    refused.  With ``layout_scope="sampling"`` the caller passes inputs already
+    in the plan's order and gets packed predictions back
+    (``sample_flux_persistent`` manages that)."""
+    _refuse(_ARGUMENT_REFUSALS, dict(layout_scope=layout_scope, backend=backend, sdpa_backend=sdpa_backend))
+    _refuse(_MODEL_REFUSALS, model)
     joint, single = list(model.transformer_blocks), list(model.single_transformer_blocks)
-    if not joint or not single:
-        raise ValueError("Both native Flux joint and single blocks are required")
     blocks = joint + single
-    originals = [block.attn.processor for block in blocks]
-    for i, (block, processor) in enumerate(zip(blocks, originals)):
-        if (isinstance(processor, PersistentFluxProcessor)
-                or getattr(processor, "_attention_backend", None) not in (None, "native")
-                or getattr(processor, "_parallel_config", None) is not None):
-            raise ValueError("Only native, non-parallel Diffusers FluxAttnProcessor is supported")
-        if (block.attn.added_kv_proj_dim is not None) != (i < len(joint)):
-            raise ValueError("Native joint/single projection types disagree with block layout")
-    info = {
-        "backend": backend,
-        "sdpa_backend": sdpa_backend,
-        "kernel_options": dict(kernel_options or {}),
-        "layout_scope": layout_scope,
-        "transformer_calls": 0,
-        "image_reorder_calls": 0,
-        "image_inverse_calls": 0,
-        "image_id_reorder_calls": 0,
-        "per_layer_image_permutations": 0,
-        "layer_calls": [0] * len(blocks),
-        "layer_phases": [i % 4 for i in range(len(blocks))],
-        "joint_layers": len(joint),
-        "single_layers": len(single),
-        "metadata_device_copies": 0,
-        "reference_masks_prepared": 0,
-        "image_layout_gather_read_write_bytes": 0,
-        "layout": "native text prefix; shared image prefix; remaining image tokens; "
-        + ("one Transformer-entry/exit gather" if layout_scope == "transformer" else "packed throughout sampling"),
-        "shared_tokens_keep_image_projections": True,
-        "native_dynamic_text_preserved": True,
-        "precision": "unchanged; native QK RMSNorm and RoPE",
-        "weights_modified": False,
-        "kernel": "sm_100a paired (hb_paired_fwd)" if backend != "sdpa_reference" else "torch SDPA, dense plan mask",
-    }
+    for i, block in enumerate(blocks):
+        _refuse(_BLOCK_REFUSALS, (block, i < len(joint)))
+    options = dict(kernel_options or {})
+    info = _info(backend, sdpa_backend, options, layout_scope, len(joint), len(single))
     bank = PlanBank(plan, info)
     info["image_order_sha256"] = bank.order_hash
-    runtime = _Runtime(model, bank, info)
-    handles = []
-    setattr(model, _ACTIVE, True)
-    try:
+    scope = _GatherAtBoundary(bank, info) if layout_scope == "transformer" else _AlreadyPacked()
+    boundary = _Boundary(model, bank, info, scope)
+    with contextlib.ExitStack() as undo:
+        setattr(model, _ACTIVE, True)
+        undo.callback(delattr, model, _ACTIVE)
+        undo.callback(bank.clear)
+        saved = [block.attn.processor for block in blocks]
+        undo.callback(lambda: [b.attn.set_processor(p) for b, p in zip(blocks, saved)])
         for i, block in enumerate(blocks):
-            block.attn.set_processor(PersistentFluxProcessor(runtime, i, backend, kernel_options or {}))
-        # outside hooks registered earlier still see raster inputs; the restore
-        # runs first so outside post-hooks see raster predictions
-        handles.append(model.register_forward_pre_hook(runtime.before, with_kwargs=True))
-        handles.append(model.register_forward_hook(runtime.after, prepend=True, always_call=True))
-        with sdpa_kernel([_SDP_BACKENDS[sdpa_backend]]):
-            yield info
-    finally:
-        for handle in handles:
-            handle.remove()
-        for block, processor in zip(blocks, originals):
-            block.attn.set_processor(processor)
-        bank.clear()
-        delattr(model, _ACTIVE)
+            block.attn.set_processor(PersistentFluxProcessor(boundary, i, backend, options))
+        # hooks registered earlier by others still see raster inputs; the exit
+        # hook goes first so their post-hooks see raster predictions
+        undo.callback(model.register_forward_pre_hook(boundary.on_entry, with_kwargs=True).remove)
+        undo.callback(model.register_forward_hook(boundary.on_exit, prepend=True, always_call=True).remove)
+        undo.enter_context(sdpa_kernel([_SDP_BACKENDS[sdpa_backend]]))
+        yield info
 
 
 __all__ = ["persistent_flux_attention", "PersistentFluxProcessor"]

@@ -308,56 +308,6 @@ __all__ = ["FluxTransformer", "FluxOutput", "DenseProcessor", "JoinedLinear", "C
            "image_ids", "step_inputs", "rotary_3axis", "parameter_count", "attention_flops_per_step"]
 
 
-def _main(argv=None):
-    """``python -m hilberta_b200.flux_model [--grid 128] [--tiles 16] [--k 3]
-    [--steps 3] [--profile]``: time one step with HilbertA attention
-    (``persistent_flux_attention(..., backend="paired")``) and with dense
-    attention on cuda:0 and, with ``--profile``, print the per-kernel device
-    times of one HilbertA step (torch.profiler)."""
-    import argparse
-
-    from .bridge_k import bridge_k_plan
-    from .flux_adapter import persistent_flux_attention
-
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--grid", type=int, default=128)
-    ap.add_argument("--tiles", type=int, default=16)
-    ap.add_argument("--k", type=int, default=3)
-    ap.add_argument("--steps", type=int, default=3)
-    ap.add_argument("--profile", action="store_true")
-    a = ap.parse_args(argv)
-    dev = torch.device("cuda", 0)
-    plan = bridge_k_plan(a.tiles, a.k, False, grid_size=a.grid)
-    torch.manual_seed(5)
-    model = FluxTransformer(device=dev)
-    x = step_inputs(a.grid, plan.text_tokens, dev)
-
-    def timed():
-        for _ in range(2):
-            model(**x)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(a.steps):
-            model(**x)
-        e1.record()
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / a.steps
-
-    with torch.inference_mode():
-        with persistent_flux_attention(model, plan, backend="paired"):
-            print(f"hilberta: {timed():.2f} ms/step")
-            if a.profile:
-                from torch.profiler import ProfilerActivity, profile
-
-                with profile(activities=[ProfilerActivity.CUDA]) as p:
-                    model(**x)
-                    torch.cuda.synchronize()
-        print(f"dense: {timed():.2f} ms/step")
-        if a.profile:
-            print(p.key_averages().table(sort_by="cuda_time_total", row_limit=20, max_name_column_width=70))
-
-
 def step_inputs(grid, text_tokens, device, batch=1, seed=6, text_dim=4096, pooled_dim=768, dtype=torch.bfloat16):
     """Seeded synthetic inputs of one denoising call, as keyword arguments."""
     g = torch.Generator().manual_seed(seed)
@@ -370,7 +320,3 @@ def step_inputs(grid, text_tokens, device, batch=1, seed=6, text_dim=4096, poole
         txt_ids=torch.zeros(text_tokens, 3, dtype=torch.int64, device=device),
         guidance=torch.full((batch,), 3.5, device=device),
     )
-
-
-if __name__ == "__main__":
-    _main()

@@ -1,129 +1,181 @@
 """One entry and one exit permutation for a whole FLUX sampling trajectory.
 
-``sample_flux_persistent(pipe, plan, ...)`` is the reference's sampling wrapper
-(hilberta/sampling_layout.py:21-165) for any pipeline with diffusers'
-``FluxPipeline`` hooks: ``prepare_latents`` (returns packed latents and their
-image position ids), ``_unpack_latents`` (called once, right before decoding),
-``transformer`` and ``scheduler``.  The wrapper replaces those two methods for the
-duration of one call:
-
-* the first ``prepare_latents`` draws the initial noise in raster order (the
-  seed keeps its meaning) and gathers latents and ids into the plan's order;
-* the transformer then runs inside ``persistent_flux_attention(...,
-  layout_scope="sampling")``: latents stay packed through every denoising step,
-  with no per-step permutation;
-* ``_unpack_latents`` gathers them back to raster order once before decoding,
-  and a latent-only return is restored explicitly.
-
-Nothing here imports diffusers; the reference's type checks on the pipeline and
-scheduler become checks of the hooks the wrapper needs and of the scheduler's
+``sample_flux_persistent(pipe, plan, ...)`` has the signature, refusals
+(exception types and messages) and boundary counters of the reference's
+sampling wrapper (hilberta/sampling_layout.py:21-148), for any pipeline with
+the hooks of diffusers' ``FluxPipeline`` that matter here: ``prepare_latents``
+(returns packed latents and their image position ids), ``_unpack_latents``
+(called once, right before decoding), ``transformer`` and ``scheduler``.  No
+diffusers import: the reference's exact-type checks on the pipeline and its
+scheduler become checks of those hooks and of the scheduler's
 ``stochastic_sampling`` flag (a stochastic sampler's noise would not follow the
 token permutation).
+
+How it is built:
+
+* ``_Trajectory`` is the layout boundary of one call, a three-state machine
+  (raster -> packed -> restored) that owns the plan's permutation per device
+  and the counters.  Its transitions are the only places tensors move: the
+  first ``prepare_latents`` result is gathered into the plan's order (noise is
+  still drawn in raster order, so a seed keeps its meaning), and the latents
+  handed to ``_unpack_latents`` (or a latent-only return) are gathered back.
+* ``_instance_override`` swaps one bound method on the pipeline instance for
+  the duration of the call and puts back exactly what was there.
+* the transformer runs inside ``persistent_flux_attention(...,
+  layout_scope="sampling")``: every denoising step reads the packed tokens in
+  place, with no per-step permutation.
 """
 
 from __future__ import annotations
+
+import contextlib
 
 import torch
 
 from .flux_adapter import persistent_flux_attention
 
+# Marker on the pipeline while a call is in flight (the reference's attribute name).
 _ACTIVE = "_flux_sampling_layout_active"
-_MISSING = object()
+_HOOKS = ("prepare_latents", "_unpack_latents", "transformer", "scheduler")
+_IP_ADAPTER_ARGUMENTS = ("ip_adapter_image", "ip_adapter_image_embeds", "negative_ip_adapter_image",
+                         "negative_ip_adapter_image_embeds")
+_PAIRED_OPTIONS = dict(global_strategy="triton", num_warps=8, num_stages=2)
 
 
-@torch.no_grad()
-def sample_flux_persistent(pipe, plan, *, backend="paired", sdpa_backend="efficient", kernel_options=None,
-                           packed_callback_on_step_end=None, **pipeline_kwargs):
-    """Run ``pipe(**pipeline_kwargs)`` in the plan's packed layout; returns
-    ``(result, info)`` with the result in public raster order."""
-    for name in ("prepare_latents", "_unpack_latents", "transformer", "scheduler"):
-        if not hasattr(pipe, name):
-            raise TypeError(f"pipeline lacks {name}: only FluxPipeline-style pipelines are supported")
-    config = getattr(pipe.scheduler, "config", {}) or {}
-    if config.get("stochastic_sampling", False):
+def _refuse_unsupported(pipe, pipeline_kwargs):
+    """Raise on a pipeline or call the wrapper cannot serve, before any work."""
+    for hook in _HOOKS:
+        if not hasattr(pipe, hook):
+            raise TypeError(f"pipeline lacks {hook}: only FluxPipeline-style pipelines are supported")
+    scheduler_config = getattr(pipe.scheduler, "config", None) or {}
+    if scheduler_config.get("stochastic_sampling", False):
         raise ValueError("Stochastic scheduler noise requires token-identity-aware RNG")
     if getattr(pipe, _ACTIVE, False):
         raise RuntimeError("Nested sampling layout is unsupported")
     if pipeline_kwargs.get("callback_on_step_end") is not None:
         raise ValueError("Use packed_callback_on_step_end: its latents are in packed image order")
-    for name in ("ip_adapter_image", "ip_adapter_image_embeds", "negative_ip_adapter_image",
-                 "negative_ip_adapter_image_embeds"):
-        if pipeline_kwargs.get(name) is not None:
-            raise ValueError("IP-adapter needs a separate layout-aware implementation")
-    if kernel_options is None and backend == "paired":
-        kernel_options = dict(global_strategy="triton", num_warps=8, num_stages=2)
-    if packed_callback_on_step_end is not None:
-        pipeline_kwargs["callback_on_step_end"] = packed_callback_on_step_end
-    order = plan.image_order.detach().cpu().clone()
-    inverse = plan.inverse_image_order.detach().cpu().clone()
-    n = int(plan.image_tokens)
-    per_device = {}
+    if any(pipeline_kwargs.get(name) is not None for name in _IP_ADAPTER_ARGUMENTS):
+        raise ValueError("IP-adapter needs a separate layout-aware implementation")
 
-    def indices(device):
-        key = str(device)
-        if key not in per_device:
-            per_device[key] = (order.to(device), inverse.to(device))
-        return per_device[key]
 
-    boundary = dict(sampling_image_reorder_calls=0, sampling_id_reorder_calls=0, sampling_inverse_calls=0,
-                    sampling_layout_read_write_bytes=0, callback_layout="packed", public_output_layout="raster")
-    originals = {name: pipe.__dict__.get(name, _MISSING) for name in ("prepare_latents", "_unpack_latents")}
-    prepare, unpack = pipe.prepare_latents, pipe._unpack_latents
+class _Trajectory:
+    """Layout state of one sampling call: ``raster`` until the entry
+    permutation, ``packed`` while denoising, ``restored`` after the exit."""
 
-    def packed_prepare(*args, **kwargs):
-        if boundary["sampling_image_reorder_calls"]:
+    def __init__(self, plan):
+        self.image_tokens = int(plan.image_tokens)
+        self._host = {"pack": plan.image_order.detach().cpu().clone(),
+                      "restore": plan.inverse_image_order.detach().cpu().clone()}
+        self._on_device = {}
+        self.state = "raster"
+        self.counters = dict(sampling_image_reorder_calls=0, sampling_id_reorder_calls=0, sampling_inverse_calls=0,
+                             sampling_layout_read_write_bytes=0, callback_layout="packed",
+                             public_output_layout="raster")
+
+    def _move(self, x, dim, direction):
+        key = (direction, str(x.device))
+        index = self._on_device.get(key)
+        if index is None:
+            index = self._on_device[key] = self._host[direction].to(x.device)
+        self.counters["sampling_layout_read_write_bytes"] += 2 * x.numel() * x.element_size()  # read + write
+        return x.index_select(dim, index)
+
+    def admit_entry(self):
+        """Called before the pipeline's own prepare_latents runs."""
+        if self.state != "raster":
             raise RuntimeError("Expected exactly one native prepare_latents call")
-        latent, ids = prepare(*args, **kwargs)
-        if latent.ndim != 3 or latent.shape[1] != n:
+
+    def enter(self, latents, ids):
+        if latents.ndim != 3 or latents.shape[1] != self.image_tokens:
             raise ValueError("Prepared image-token count does not match the plan")
-        if ids.ndim not in (2, 3) or ids.shape[-2:] != (n, 3):
+        if ids.ndim not in (2, 3) or ids.shape[-2:] != (self.image_tokens, 3):
             raise ValueError("Prepared image position IDs do not match the plan")
-        latent = latent.index_select(1, indices(latent.device)[0])
-        ids = ids.index_select(ids.ndim - 2, indices(ids.device)[0])
-        boundary["sampling_image_reorder_calls"] += 1
-        boundary["sampling_id_reorder_calls"] += 1
-        boundary["sampling_layout_read_write_bytes"] += 2 * (
-            latent.numel() * latent.element_size() + ids.numel() * ids.element_size())
-        return latent, ids
+        packed = (self._move(latents, 1, "pack"), self._move(ids, ids.ndim - 2, "pack"))
+        self.counters["sampling_image_reorder_calls"] += 1
+        self.counters["sampling_id_reorder_calls"] += 1
+        self.state = "packed"
+        return packed
 
-    def restore(latent):
-        if boundary["sampling_image_reorder_calls"] != 1 or boundary["sampling_inverse_calls"]:
+    def leave(self, latents):
+        if self.state != "packed":
             raise RuntimeError("Expected exactly one sampling entry and exit permutation")
-        if latent.ndim != 3 or latent.shape[1] != n:
+        if latents.ndim != 3 or latents.shape[1] != self.image_tokens:
             raise ValueError("Final latent image-token count does not match the plan")
-        out = latent.index_select(1, indices(latent.device)[1])
-        boundary["sampling_inverse_calls"] += 1
-        boundary["sampling_layout_read_write_bytes"] += 2 * latent.numel() * latent.element_size()
-        return out
+        raster = self._move(latents, 1, "restore")
+        self.counters["sampling_inverse_calls"] += 1
+        self.state = "restored"
+        return raster
 
-    def raster_unpack(latents, *args, **kwargs):
-        return unpack(restore(latents), *args, **kwargs)
+    def close(self):
+        if self.state != "restored":
+            raise RuntimeError("Native pipeline did not pass the sampling exit boundary")
 
-    setattr(pipe, _ACTIVE, True)
+
+@contextlib.contextmanager
+def _instance_override(obj, name, value):
+    """Set ``obj.name`` for the duration of the block, then put back exactly
+    what the instance had: its own attribute, or none (so the class's method
+    shows through again)."""
+    own = vars(obj)
+    had, old = name in own, own.get(name)
+    setattr(obj, name, value)
     try:
-        with persistent_flux_attention(pipe.transformer, plan, backend=backend, sdpa_backend=sdpa_backend,
-                                       kernel_options=kernel_options, layout_scope="sampling") as info:
-            pipe.prepare_latents = packed_prepare
-            pipe._unpack_latents = raster_unpack
-            result = pipe(**pipeline_kwargs)
-            if pipeline_kwargs.get("output_type") == "latent":
-                if hasattr(result, "images"):
-                    result = type(result)(images=restore(result.images))
-                elif isinstance(result, tuple) and len(result) == 1:
-                    result = (restore(result[0]),)
-                else:
-                    raise TypeError("Unexpected native Flux latent return type")
-            if boundary["sampling_inverse_calls"] != 1:
-                raise RuntimeError("Native pipeline did not pass the sampling exit boundary")
-            info.update(boundary)
-            return result, info
+        yield
     finally:
-        for name, old in originals.items():
-            if old is _MISSING:
-                pipe.__dict__.pop(name, None)
-            else:
-                setattr(pipe, name, old)
-        delattr(pipe, _ACTIVE)
+        if had:
+            setattr(obj, name, old)
+        else:
+            own.pop(name, None)
+
+
+def _latent_return(result, leave):
+    """A latent-only pipeline return with its latents back in raster order."""
+    if hasattr(result, "images"):
+        return type(result)(images=leave(result.images))
+    if isinstance(result, tuple) and len(result) == 1:
+        return (leave(result[0]),)
+    raise TypeError("Unexpected native Flux latent return type")
+
+
+@torch.no_grad()
+def sample_flux_persistent(pipe, plan, *, backend="paired", sdpa_backend="efficient", kernel_options=None,
+                           packed_callback_on_step_end=None, **pipeline_kwargs):
+    """Run ``pipe(**pipeline_kwargs)`` with the image tokens in the plan's packed
+    order for the whole trajectory; returns ``(result, info)``, the result in
+    public raster order.  ``packed_callback_on_step_end`` is passed to the
+    pipeline as its ``callback_on_step_end`` and sees packed latents; a plain
+    ``callback_on_step_end`` is refused.  Inference only, single-threaded,
+    reversible: the pipeline's methods are as before afterwards."""
+    _refuse_unsupported(pipe, pipeline_kwargs)
+    if kernel_options is None and backend == "paired":
+        kernel_options = dict(_PAIRED_OPTIONS)
+    call = dict(pipeline_kwargs)
+    if packed_callback_on_step_end is not None:
+        call["callback_on_step_end"] = packed_callback_on_step_end
+    trajectory = _Trajectory(plan)
+    native_prepare, native_unpack = pipe.prepare_latents, pipe._unpack_latents
+
+    def prepare_packed(*args, **kwargs):
+        trajectory.admit_entry()
+        return trajectory.enter(*native_prepare(*args, **kwargs))
+
+    def unpack_raster(latents, *args, **kwargs):
+        return native_unpack(trajectory.leave(latents), *args, **kwargs)
+
+    with contextlib.ExitStack() as stack:
+        setattr(pipe, _ACTIVE, True)
+        stack.callback(delattr, pipe, _ACTIVE)
+        info = stack.enter_context(persistent_flux_attention(
+            pipe.transformer, plan, backend=backend, sdpa_backend=sdpa_backend, kernel_options=kernel_options,
+            layout_scope="sampling"))
+        stack.enter_context(_instance_override(pipe, "prepare_latents", prepare_packed))
+        stack.enter_context(_instance_override(pipe, "_unpack_latents", unpack_raster))
+        result = pipe(**call)
+        if call.get("output_type") == "latent":
+            result = _latent_return(result, trajectory.leave)
+        trajectory.close()
+        info.update(trajectory.counters)
+        return result, info
 
 
 __all__ = ["sample_flux_persistent"]
