@@ -9,17 +9,20 @@
 //
 // B200 design (one CTA = 8 warps, two CTAs per SM, persistent):
 //   warp 0  item fetcher (atomic work counter; global-row chunks first, then
-//           ordinary pair-rows head-major) + TMA loads of Q and K (3 stages)
+//           ordinary pair-rows head-major): decodes each item and its first 32
+//           flags into a two-slot shared ring; TMA loads of Q and K (3 stages)
 //   warp 1  TMA loads of V (2 stages)
 //   warp 2  single-thread tcgen05.mma issuer: S = Q K^T (SS, 128x64x16 steps)
 //           into TMEM, O += P V (TS: P read from TMEM, V MN-major from SMEM),
 //           each issued as soon as its inputs are ready (non-blocking polls)
-//   warp 3  TMEM allocator
+//   warp 3  TMEM allocator; in the fused all-gather, pushes rows to the peers
 //   warps 4-7  softmax: one TMEM lane (query row) per thread, exp2 online
 //           softmax with lazy O rescaling (only when the running max grows by
-//           more than 2^8), P written back into the S columns as 16-bit pairs,
-//           epilogue O / l -> the output (or this rank's rows to every rank's
-//           output, fused all-gather), or a chunk's partial for split rows.
+//           more than 2^8), P written back into the S columns as 16-bit pairs.
+//           An item's epilogue (O / l -> the output with 32-byte stores, or the
+//           fused all-gather's hand-off, or a chunk's partial for split rows)
+//           runs after the NEXT item's first step, when its last PV has long
+//           completed and the next first PV is the only MMA waiting for O.
 // TMEM per CTA: S0 [0,64) S1 [64,128) O [128,128+D) (256 columns; two CTAs fill
 // the 512-column TMEM of an SM).  Tiles use the 128-byte swizzle end to end;
 // mbarriers live after the tiles in the (1024-byte aligned) dynamic region.
@@ -104,6 +107,14 @@ constexpr int CHUNK_BLOCKS = 32;                          // target key blocks p
 constexpr int64_t MIN_GROUP_PARTIAL = 2 * (128 * 64 + 256) * 4;  // smallest partials of one split group
 inline int64_t counter_bytes(int64_t ws) { return ((4 * (ws / MIN_GROUP_PARTIAL + 1) + 255) / 256) * 256; }
 
+// One work item handed from the fetcher (warp 0) to the other roles: its index,
+// its block count and, for an ordinary pair-row, the flags of its first 32
+// entries, so no consumer makes a dependent global load when an item starts.
+struct ItemSlot {
+    int item, n;
+    int flags[32];
+};
+
 template <int D>
 struct Cfg {
     static constexpr int SLABS = D / 64;           // 64-element (128-byte) column slabs
@@ -117,11 +128,11 @@ struct Cfg {
     // shared memory, so the region starts 1024-byte aligned with no padding:
     // two CTAs with three K stages fit in an SM's 228 KB).
     struct Ctl {
-        uint64_t q_full, q_empty, o_done, o_empty, drain, wg;
+        uint64_t q_full, q_empty, o_done, o_empty, drain, wg, final_done;
         uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
         uint64_t s_full[2], p_full[2], item_full[2], item_empty[2];
         uint64_t push_full[2], push_empty[2];  // fused all-gather: finished items handed to warp 3
-        int item_slot[2];
+        ItemSlot slots[2];
         int push_item[2];
         uint32_t tmem_base;
         int abort;
@@ -141,13 +152,6 @@ struct Cfg {
 constexpr int MODE_TILED = 0, MODE_ROWS = 1, MODE_SQUARES = 2;
 
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8 between rescales
-// One in POLY_EXP2_EVERY element pairs of a score row takes 2^x from ex2_poly2
-// (FMA pipe) instead of MUFU ex2; a power of two, 0 = MUFU only (measured
-// fastest while the kernel is latency- rather than MUFU-bound).
-#ifndef HB_POLY_EXP2_EVERY
-#define HB_POLY_EXP2_EVERY 0
-#endif
-constexpr int POLY_EXP2_EVERY = HB_POLY_EXP2_EVERY;
 
 struct Item {
     int b, h, qrow0, row, n;
@@ -156,7 +160,9 @@ struct Item {
     bool global, split;
 };
 
-__device__ __forceinline__ Item decode_item(const FwdParams& p, int item, bool report) {
+// Work item -> (batch, head, query rows, key blocks), given its block count n
+// (pure arithmetic: no loads).
+__device__ __forceinline__ Item decode_item_n(const FwdParams& p, int item, int n) {
     Item w;
     if (item < p.n_global_items) {
         // (bh, chunk, global pair-row): the global rows reading the same key blocks
@@ -170,7 +176,6 @@ __device__ __forceinline__ Item decode_item(const FwdParams& p, int item, bool r
         w.qrow0 = gp * 128;
         w.row = 0;
         w.blk0 = c * p.chunk;
-        w.n = min(p.chunk, p.nkb - w.blk0);
         w.chunk = c;
         w.group = bh * p.g_rows + gp;
         w.global = true;
@@ -186,12 +191,23 @@ __device__ __forceinline__ Item decode_item(const FwdParams& p, int item, bool r
         w.h = bh % p.H;
         w.row = t % p.o_rows;
         w.qrow0 = p.G + w.row * 128;
-        const int c = p.counts[w.row];
-        if (report && (c < 1 || c > p.W)) atomicOr(&p.ws[2], HB_DEV_BAD_COUNT);
-        w.n = c < 1 ? 1 : (c > p.W ? p.W : c);
         w.global = false;
     }
+    w.n = n;
     return w;
+}
+
+// Block count of a work item: a global chunk's from the split, an ordinary
+// pair-row's from the metadata (clamped to [1, W]; out of range is reported).
+__device__ __forceinline__ int item_blocks(const FwdParams& p, int item, bool report) {
+    if (item < p.n_global_items) {
+        const int c = (item / p.g_rows) % p.n_chunks;
+        return min(p.chunk, p.nkb - c * p.chunk);
+    }
+    const int row = (item - p.n_global_items) % p.o_rows;
+    const int c = p.counts[row];
+    if (report && (c < 1 || c > p.W)) atomicOr(&p.ws[2], HB_DEV_BAD_COUNT);
+    return c < 1 ? 1 : (c > p.W ? p.W : c);
 }
 
 __device__ __forceinline__ void tma_coords(const int32_t* perm, int n, int h, int b, int& c1, int& c2, int& c3) {
@@ -294,7 +310,7 @@ __device__ __forceinline__ void load_block_sq(const FwdParams& p, const CUtensor
 // mode).  WHICH = 0: Q + K, 1: V.
 template <int D, int WHICH, int MODE>
 __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t* bar_item_full,
-                         uint64_t* bar_item_empty, int* item_slot, uint64_t* bar_q_full, uint64_t* bar_q_empty,
+                         uint64_t* bar_item_empty, ItemSlot* slots, uint64_t* bar_q_full, uint64_t* bar_q_empty,
                          uint64_t* bar_full, uint64_t* bar_empty, volatile int* abort_flag) {
     using C = Cfg<D>;
     constexpr int STAGES = WHICH == 0 ? C::KS : C::VS;
@@ -312,23 +328,36 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
     for (int it = 0; ok; it++) {
         const int slot = it & 1;
         int item;
+        Item w;
         if (WHICH == 0) {
             if (!warp_wait(&bar_item_empty[slot], ((it >> 1) & 1) ^ 1, abort_flag, p.timeout)) break;
             item = 0;
-            if (lane == 0) {
-                item = atomicAdd(&p.ws[0], 1);
-                item_slot[slot] = item;
-                mbar_arrive(&bar_item_full[slot]);
-            }
+            if (lane == 0) item = atomicAdd(&p.ws[0], 1);
             item = __shfl_sync(FULL, item, 0);
+            // decode (the block count of an ordinary row) and the first 32 flags
+            // before publishing the item: one warp-wide load each
+            int n = 0, fl = 0;
+            if (item < p.num_items) {
+                w = decode_item_n(p, item, item_blocks(p, item, lane == 0));
+                n = w.n;
+                fl = w.global ? 3 : (lane < w.n ? p.flags[(int64_t)w.row * p.W + lane] : 0);
+            }
+            slots[slot].flags[lane] = fl;
+            if (lane == 0) {
+                slots[slot].item = item;
+                slots[slot].n = n;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_item_full[slot]);
         } else {
             if (!warp_wait(&bar_item_full[slot], (it >> 1) & 1, abort_flag, p.timeout)) break;
-            item = item_slot[slot];
+            item = slots[slot].item;
+            const int n = slots[slot].n;
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_item_empty[slot]);
+            if (item < p.num_items) w = decode_item_n(p, item, n);
         }
         if (item >= p.num_items) break;
-        const Item w = decode_item(p, item, WHICH == 0 && lane == 0);
         if (WHICH == 0) {
             if (!warp_wait(bar_q_empty, (it & 1) ^ 1, abort_flag, p.timeout)) break;
             if constexpr (MODE == MODE_ROWS) {
@@ -407,10 +436,10 @@ __device__ void producer(const FwdParams& p, uint8_t* sQ, uint8_t* sKV, uint64_t
 
 template <int D, bool BF16>
 __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8_t* sK, uint8_t* sV,
-                           uint64_t* bar_item_full, uint64_t* bar_item_empty, int* item_slot, uint64_t* bar_q_full,
+                           uint64_t* bar_item_full, uint64_t* bar_item_empty, ItemSlot* slots, uint64_t* bar_q_full,
                            uint64_t* bar_q_empty, uint64_t* bar_k_full, uint64_t* bar_k_empty, uint64_t* bar_v_full,
                            uint64_t* bar_v_empty, uint64_t* bar_s_full, uint64_t* bar_p_full, uint64_t* bar_o_done,
-                           uint64_t* bar_o_empty, uint64_t* bar_drain, volatile int* abort_flag) {
+                           uint64_t* bar_o_empty, uint64_t* bar_drain, uint64_t* bar_final, volatile int* abort_flag) {
     using C = Cfg<D>;
     constexpr uint32_t IDESC_QK = idesc_f16(128, 64, BF16, false);
     constexpr uint32_t IDESC_PV = idesc_f16(128, D, BF16, true);
@@ -425,10 +454,14 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
     for (int it = 0; ok; it++) {
         const int slot = it & 1;
         if (!mbar_wait(&bar_item_full[slot], (it >> 1) & 1, abort_flag, p.timeout)) break;
-        const int item = item_slot[slot];
+        const int item = slots[slot].item;
+        const int n_item = slots[slot].n;
         mbar_arrive(&bar_item_empty[slot]);
-        if (item >= p.num_items) break;
-        const Item w = decode_item(p, item, false);
+        if (item >= p.num_items) {
+            tc_commit(bar_final);  // completes once every MMA issued by this CTA has
+            break;
+        }
+        const Item w = decode_item_n(p, item, n_item);
         if (!mbar_wait(bar_q_full, it & 1, abort_flag, p.timeout)) break;
         tc_fence_after();
         // Issue S_js = Q K_js^T and O += P_jp V_jp in whichever order their inputs
@@ -525,7 +558,7 @@ __device__ void pusher(const FwdParams& p, uint64_t* bar_full, uint64_t* bar_emp
         if (!warp_wait(&bar_full[ps], (k >> 1) & 1, abort_flag, p.timeout)) return;
         const int item = push_item[ps];
         if (item < 0) return;
-        const Item w = decode_item(p, item, false);
+        const Item w = decode_item_n(p, item, 0);  // rows only
         const int64_t hb_off = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh;
         const int row0 = w.qrow0 + lane / CPR;
         // loads in batches ahead of their stores: the destinations could alias the
@@ -565,12 +598,28 @@ __device__ __forceinline__ bool enqueue_push(const FwdParams& p, uint64_t* bar_f
     return true;
 }
 
+// 32-byte global store (st.global.cs.v8.b32): one full sector per lane.
+__device__ __forceinline__ void st_cs_v8(void* dst, const uint32_t* v) {
+    asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+                 "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
+// The softmax warpgroup's view of a finished item whose output is still to be
+// written (its epilogue runs after the next item's first step).
+struct Pending {
+    int item, n;       // the item (decoded again when its epilogue runs: fewer live registers)
+    float m, l;
+    uint32_t last_pv;  // global index of the item's last PV (o_done phase)
+};
+
 template <int D, bool BF16, int MODE>
 __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_item_full, uint64_t* bar_item_empty,
-                             int* item_slot, uint64_t* bar_s_full, uint64_t* bar_p_full, uint64_t* bar_o_done,
+                             ItemSlot* slots, uint64_t* bar_s_full, uint64_t* bar_p_full, uint64_t* bar_o_done,
                              uint64_t* bar_o_empty, uint64_t* bar_wg, int* wg_flag, uint64_t* bar_push_full,
-                             uint64_t* bar_push_empty, int* push_item, volatile int* abort_flag) {
+                             uint64_t* bar_push_empty, int* push_item, uint64_t* bar_final, volatile int* abort_flag) {
     using C = Cfg<D>;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     const int r = threadIdx.x - 128;  // query row within the tile == TMEM lane
     uint32_t npush = 0;               // items handed to the pusher (fused all-gather)
     uint32_t wg_uses = 0;             // phases of bar_wg (the 4 softmax warps) used so far
@@ -578,118 +627,18 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
     const int half = r >> 6;
     const uint32_t t_lane = tmem + ((uint32_t)((r >> 5) * 32) << 16);
     const float sl2 = p.scale_log2;
-    uint32_t g = 0;
-    for (int it = 0;; it++) {
-        const int slot = it & 1;
-        if (!warp_wait(&bar_item_full[slot], (it >> 1) & 1, abort_flag, p.timeout)) return;
-        const int item = item_slot[slot];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar_item_empty[slot]);
-        if (item >= p.num_items) {
-            if (p.n_out > 1) enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, -1, abort_flag);
-            return;
-        }
-        const Item w = decode_item(p, item, false);
-        float m = -INFINITY, l = 0.f;
-        int chunk = 0;
-        for (int j = 0; j < w.n; j++) {
-            const uint32_t gg = g + j;
-            const int buf = gg & 1;
-            if (!w.global && (j & 31) == 0) {
-                const int jj = j + lane;
-                chunk = jj < w.n ? p.flags[(int64_t)w.row * p.W + jj] : 0;
-            }
-            const int fl = w.global ? 3 : __shfl_sync(FULL, chunk, j & 31);
-            const bool allowed = (fl >> half) & 1;  // uniform per warp
-            if (!warp_wait(&bar_s_full[buf], (gg >> 1) & 1, abort_flag, p.timeout)) return;
-            tc_fence_after();
-            const uint32_t s_addr = t_lane + C::S_COL0 + buf * 64;
-            uint32_t pk[32];
-            float m_new = m, alpha = 1.f;
-            if (allowed) {
-                uint32_t s[64];
-                tmem_ld64(s_addr, s);
-                // row max: 3-input max over four independent chains
-                float a0 = fmaxf(__uint_as_float(s[0]), __uint_as_float(s[1]));
-                float a1 = fmaxf(__uint_as_float(s[2]), __uint_as_float(s[3]));
-                float a2 = fmaxf(__uint_as_float(s[4]), __uint_as_float(s[5]));
-                float a3 = fmaxf(__uint_as_float(s[6]), __uint_as_float(s[7]));
-#pragma unroll
-                for (int i = 8; i < 64; i += 8) {
-                    a0 = fmax3(a0, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
-                    a1 = fmax3(a1, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
-                    a2 = fmax3(a2, __uint_as_float(s[i + 4]), __uint_as_float(s[i + 5]));
-                    a3 = fmax3(a3, __uint_as_float(s[i + 6]), __uint_as_float(s[i + 7]));
-                }
-                const float mx = fmaxf(fmax3(a0, a1, a2), a3) * sl2;
-                if (mx > m + RESCALE_THRESHOLD) {
-                    m_new = mx;
-                    alpha = ex2(m - m_new);  // 0 when m == -inf
-                }
-                // p = 2^(s*scale*log2e - m): packed FMA for the argument, MUFU ex2,
-                // packed adds into four partial row sums
-                const uint64_t scale2 = f2_pack(sl2, sl2);
-                const uint64_t neg_m2 = f2_pack(-m_new, -m_new);
-                uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
-                                               scale2, neg_m2);
-                    float x0, x1, p0, p1;
-                    f2_unpack(x2, x0, x1);
-                    if (POLY_EXP2_EVERY > 0 && (i & (POLY_EXP2_EVERY - 1)) == POLY_EXP2_EVERY - 1) {
-                        ex2_poly2(x0, x1, p0, p1);
-                    } else {
-                        p0 = ex2(x0);
-                        p1 = ex2(x1);
-                    }
-                    acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
-                    pk[i] = pack2<BF16>(p0, p1);
-                }
-                float s0, s1, s2, s3;
-                f2_unpack(f2_add(acc[0], acc[1]), s0, s1);
-                f2_unpack(f2_add(acc[2], acc[3]), s2, s3);
-                l = l * alpha + ((s0 + s1) + (s2 + s3));
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; i++) pk[i] = 0u;
-            }
-            tmem_st32(s_addr, pk);
-            // O may only be rescaled once PV_{gg-1} has completed.  S_gg being ready
-            // means PV_{gg-2} completed (it was issued first), and PV_gg waits for
-            // this step's P, so o_done is at phase gg-1 or gg: waiting on the parity
-            // of gg-1 is exact without having waited the earlier phases.  Only a
-            // rescale needs that wait, and the item's last step, after which the
-            // epilogue waits on the last PV with the same two-phase guarantee.
-            const bool need = (m_new != m) && (m != -INFINITY);
-            const bool rescale = __any_sync(FULL, need);
-            if (j > 0 && (rescale || j == w.n - 1)) {
-                if (!warp_wait(bar_o_done, (gg - 1) & 1, abort_flag, p.timeout)) return;
-                tc_fence_after();
-            }
-            if (rescale) {
-                const float a = need ? alpha : 1.f;
-#pragma unroll
-                for (int c = 0; c < D / 32; c++) {
-                    uint32_t o[32];
-                    tmem_ld32(t_lane + C::O_COL + 32 * c, o);
-#pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
-                    tmem_st32(t_lane + C::O_COL + 32 * c, o);
-                }
-            }
-            m = m_new;
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar_p_full[buf]);
-        }
-        // epilogue: O / l -> global (or, for a chunk of a split global row, the
-        // chunk's unnormalised O with its m and l -> partial, merged by the last chunk)
-        const uint32_t gl = g + w.n - 1;
-        if (!warp_wait(bar_o_done, gl & 1, abort_flag, p.timeout)) return;
+
+    // Epilogue of a finished item: O / l -> the output (or, for a chunk of a
+    // split global row, the chunk's unnormalised O with its m and l -> partial,
+    // merged by the last chunk).  Waits for the item's last PV, whose o_done
+    // phase is exact here: PV_{last-1} has completed (the next item's first S
+    // was ready, and MMAs complete in issue order; on the way out it is waited
+    // for explicitly) and the next PV needs this epilogue's o_empty first.  O's
+    // TMEM is free for the next item's first PV once it returns.
+    auto finish = [&](const Pending& pd) -> bool {
+        const Item w = decode_item_n(p, pd.item, pd.n);
+        if (!warp_wait(bar_o_done, pd.last_pv & 1, abort_flag, p.timeout)) return false;
         tc_fence_after();
-        using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
         int orow = w.qrow0 + r;  // output token row of this thread's query
         if constexpr (MODE == MODE_ROWS) orow = p.row_map[orow];
         if constexpr (MODE == MODE_SQUARES) {
@@ -701,26 +650,27 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
         }
         const bool row_ok = orow >= 0 && orow < p.N;  // a bad map entry drops the row, never stores out of range
         const int64_t ooff = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh + (int64_t)(row_ok ? orow : 0) * p.o_sn;
-        // every destination has the same address residue mod 16 (checked on the host)
-        const bool vec = (reinterpret_cast<uintptr_t>(reinterpret_cast<T*>(p.outs[0]) + ooff) & 15) == 0;
+        // every destination has the same address residue mod 32 (checked on the host)
+        const uintptr_t addr0 = reinterpret_cast<uintptr_t>(reinterpret_cast<T*>(p.outs[0]) + ooff);
+        const bool vec = (addr0 & 15) == 0, vec32 = (addr0 & 31) == 0;
         // Rows are written to this rank's output first (lane = row); in the fused
         // all-gather the item is then handed to warp 3 (pusher), which copies the
-        // rows to the other ranks while this warp goes on with the next item.
+        // rows to the other ranks while this warp goes on.
         const bool push = p.n_out > 1 && vec;
-        auto store_row = [&](int c, const float* vals) {  // 32 output columns from 32 fp32 values
-            uint32_t packed[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) packed[i] = pack2<BF16>(vals[2 * i], vals[2 * i + 1]);
+        auto store32 = [&](int c0, const uint32_t (&packed)[16]) {  // 32 output columns, packed 16-bit pairs
             for (int d = 0; d < p.n_out && row_ok; d++) {
                 if (d != p.rank && push) continue;
-                T* orow = reinterpret_cast<T*>(p.outs[d]) + ooff;
-                if (vec) {
-                    uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+                T* orow_p = reinterpret_cast<T*>(p.outs[d]) + ooff + c0;
+                if (vec32) {  // written once, read by the next layer: do not keep in L2 over K/V
+                    st_cs_v8(orow_p, packed);
+                    st_cs_v8(orow_p + 16, packed + 8);
+                } else if (vec) {
+                    uint4* dst = reinterpret_cast<uint4*>(orow_p);
 #pragma unroll
-                    for (int i = 0; i < 4; i++)  // written once, read by the next layer: do not keep in L2 over K/V
+                    for (int i = 0; i < 4; i++)
                         __stcs(dst + i, make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]));
                 } else {
-                    uint16_t* dst = reinterpret_cast<uint16_t*>(orow + 32 * c);
+                    uint16_t* dst = reinterpret_cast<uint16_t*>(orow_p);
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         dst[2 * i] = (uint16_t)(packed[i] & 0xffffu);
@@ -730,20 +680,22 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             }
         };
         if (!w.split) {
-            const float inv = 1.f / l;
+            const float inv = 1.f / pd.l;
 #pragma unroll
             for (int c = 0; c < D / 32; c++) {
                 uint32_t o[32];
                 tmem_ld32(t_lane + C::O_COL + 32 * c, o);
-                float vals[32];
+                uint32_t packed[16];
 #pragma unroll
-                for (int i = 0; i < 32; i++) vals[i] = __uint_as_float(o[i]) * inv;
-                store_row(c, vals);
+                for (int i = 0; i < 16; i++)
+                    packed[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+                store32(32 * c, packed);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_o_empty);
-            if (push && !enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, item, abort_flag)) return;
+            if (push && !enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, pd.item, abort_flag))
+                return false;
         } else {
             constexpr int PSTRIDE = 128 * D + 256;
             float* rec = p.partial + ((int64_t)w.group * p.n_chunks + w.chunk) * PSTRIDE;
@@ -757,8 +709,8 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                     dst[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
                                          __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
             }
-            rec[128 * D + r] = m;
-            rec[128 * D + 128 + r] = l;
+            rec[128 * D + r] = pd.m;
+            rec[128 * D + 128 + r] = pd.l;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_o_empty);  // O's TMEM may be reused now
@@ -766,7 +718,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             // all 128 rows written -> count this chunk; the last chunk of the row merges
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_wg);
-            if (!warp_wait(bar_wg, wg_uses & 1, abort_flag, p.timeout)) return;
+            if (!warp_wait(bar_wg, wg_uses & 1, abort_flag, p.timeout)) return false;
             wg_uses++;
             if (r == 0) {
                 const int done = atomicAdd(&p.chunk_cnt[w.group], 1);
@@ -776,7 +728,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_wg);
-            if (!warp_wait(bar_wg, wg_uses & 1, abort_flag, p.timeout)) return;
+            if (!warp_wait(bar_wg, wg_uses & 1, abort_flag, p.timeout)) return false;
             wg_uses++;
             if (*wg_flag) {
                 __threadfence();
@@ -806,14 +758,146 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                             vals[4 * i + 3] += wt[k] * v4.w;
                         }
                     }
+                    uint32_t packed[16];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) vals[i] *= inv;
-                    store_row(c, vals);
+                    for (int i = 0; i < 16; i++) packed[i] = pack2<BF16>(vals[2 * i] * inv, vals[2 * i + 1] * inv);
+                    store32(32 * c, packed);
                 }
-                if (push && !enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, item, abort_flag))
-                    return;
+                if (push && !enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, pd.item, abort_flag))
+                    return false;
             }
         }
+        return true;
+    };
+
+    Pending pend;
+    bool pending = false;
+    uint32_t g = 0;
+    for (int it = 0;; it++) {
+        const int slot = it & 1;
+        if (!warp_wait(&bar_item_full[slot], (it >> 1) & 1, abort_flag, p.timeout)) return;
+        const int item = slots[slot].item;
+        const int n_item = slots[slot].n;
+        int chunk = slots[slot].flags[lane];  // lane l: flags of entry l
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_item_empty[slot]);
+        if (item >= p.num_items) {
+            // No later S was waited for: wait until every MMA of this CTA has
+            // completed (the issuer's final commit), then finish() finds the
+            // last PV's o_done phase complete and no later one.
+            if (pending && !warp_wait(bar_final, 0, abort_flag, p.timeout)) return;
+            if (pending && !finish(pend)) return;
+            if (p.n_out > 1) enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, -1, abort_flag);
+            return;
+        }
+        const Item w = decode_item_n(p, item, n_item);
+        float m = -INFINITY, l = 0.f;
+        int next_chunk = 0;
+        // one softmax step: scores S_j -> P_j (and the running max / sum)
+        auto step = [&](int j) -> bool {
+            const uint32_t gg = g + j;
+            const int buf = gg & 1;
+            if (!w.global) {
+                if ((j & 31) == 0 && j > 0) chunk = next_chunk;
+                if ((j & 31) == 16 && j + 16 < w.n) {  // flags of entries j+16 .. j+47, a step ahead of use
+                    const int jj = j + 16 + lane;
+                    next_chunk = jj < w.n ? p.flags[(int64_t)w.row * p.W + jj] : 0;
+                }
+            }
+            const int fl = w.global ? 3 : __shfl_sync(FULL, chunk, j & 31);
+            const bool allowed = (fl >> half) & 1;  // uniform per warp
+            if (!warp_wait(&bar_s_full[buf], (gg >> 1) & 1, abort_flag, p.timeout)) return false;
+            tc_fence_after();
+            const uint32_t s_addr = t_lane + C::S_COL0 + buf * 64;
+            uint32_t pk[32];
+            float m_new = m, alpha = 1.f;
+            if (allowed) {
+                uint32_t s_[64];
+                tmem_ld64(s_addr, s_);
+                // row max: 3-input max over four independent chains
+                float a0 = fmaxf(__uint_as_float(s_[0]), __uint_as_float(s_[1]));
+                float a1 = fmaxf(__uint_as_float(s_[2]), __uint_as_float(s_[3]));
+                float a2 = fmaxf(__uint_as_float(s_[4]), __uint_as_float(s_[5]));
+                float a3 = fmaxf(__uint_as_float(s_[6]), __uint_as_float(s_[7]));
+#pragma unroll
+                for (int i = 8; i < 64; i += 8) {
+                    a0 = fmax3(a0, __uint_as_float(s_[i]), __uint_as_float(s_[i + 1]));
+                    a1 = fmax3(a1, __uint_as_float(s_[i + 2]), __uint_as_float(s_[i + 3]));
+                    a2 = fmax3(a2, __uint_as_float(s_[i + 4]), __uint_as_float(s_[i + 5]));
+                    a3 = fmax3(a3, __uint_as_float(s_[i + 6]), __uint_as_float(s_[i + 7]));
+                }
+                const float mx = fmaxf(fmax3(a0, a1, a2), a3) * sl2;
+                if (mx > m + RESCALE_THRESHOLD) {
+                    m_new = mx;
+                    alpha = ex2(m - m_new);  // 0 when m == -inf
+                }
+                // p = 2^(s*scale*log2e - m): packed FMA for the argument, MUFU ex2,
+                // packed adds into four partial row sums
+                const uint64_t scale2 = f2_pack(sl2, sl2);
+                const uint64_t neg_m2 = f2_pack(-m_new, -m_new);
+                uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s_[2 * i]), __uint_as_float(s_[2 * i + 1])),
+                                               scale2, neg_m2);
+                    float x0, x1;
+                    f2_unpack(x2, x0, x1);
+                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
+                    pk[i] = pack2<BF16>(p0, p1);
+                }
+                float s0, s1, s2, s3;
+                f2_unpack(f2_add(acc[0], acc[1]), s0, s1);
+                f2_unpack(f2_add(acc[2], acc[3]), s2, s3);
+                l = l * alpha + ((s0 + s1) + (s2 + s3));
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) pk[i] = 0u;
+            }
+            tmem_st32(s_addr, pk);
+            // O may only be rescaled once PV_{gg-1} has completed.  S_gg being ready
+            // means PV_{gg-2} completed (it was issued first), and PV_gg waits for
+            // this step's P, so o_done is at phase gg-1 or gg: waiting on the parity
+            // of gg-1 is exact without having waited the earlier phases.  Only a
+            // rescale needs that wait (step 0 of an item never rescales).
+            const bool need = (m_new != m) && (m != -INFINITY);
+            const bool rescale = __any_sync(FULL, need);
+            if (rescale) {
+                if (!warp_wait(bar_o_done, (gg - 1) & 1, abort_flag, p.timeout)) return false;
+                tc_fence_after();
+                const float a = need ? alpha : 1.f;
+#pragma unroll
+                for (int c = 0; c < D / 32; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(t_lane + C::O_COL + 32 * c, o);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
+                    tmem_st32(t_lane + C::O_COL + 32 * c, o);
+                }
+            }
+            m = m_new;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_p_full[buf]);
+            return true;
+        };
+        // step 0, then the previous item's epilogue (after this item's first P is
+        // handed over: its last PV has had a step to complete, and this item's
+        // first PV, which needs O's TMEM, follows right after), then the rest
+        if (!step(0)) return;
+        if (pending) {
+            if (!finish(pend)) return;
+            pending = false;
+        }
+        for (int j = 1; j < w.n; j++)
+            if (!step(j)) return;
+        pend.n = w.n;
+        pend.item = item;
+        pend.m = m;
+        pend.l = l;
+        pend.last_pv = g + w.n - 1;
+        pending = true;
         g += w.n;
     }
 }
@@ -857,7 +941,7 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
     uint64_t *bar_v_full = ctl->v_full, *bar_v_empty = ctl->v_empty;
     uint64_t *bar_s_full = ctl->s_full, *bar_p_full = ctl->p_full;
     uint64_t *bar_item_full = ctl->item_full, *bar_item_empty = ctl->item_empty;
-    int* item_slot = ctl->item_slot;
+    ItemSlot* slots = ctl->slots;
     uint32_t& tmem_base_sh = ctl->tmem_base;
     int& abort_sh = ctl->abort;
     int& wg_flag = ctl->wg_flag;
@@ -870,6 +954,7 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
         mbar_init(&bar_o_done, 1);
         mbar_init(&bar_o_empty, 4);
         mbar_init(&bar_drain, 1);
+        mbar_init(&ctl->final_done, 1);
         mbar_init(&bar_wg, 4);
         for (int i = 0; i < C::KS; i++) {
             mbar_init(&bar_k_full[i], 1);
@@ -905,20 +990,20 @@ __global__ void __launch_bounds__(256, 2) k_paired_fwd(const __grid_constant__ F
     const uint32_t tmem = tmem_base_sh;
 
     if (warp == 0) {
-        producer<D, 0, MODE>(p, sQ, sK, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_k_full,
+        producer<D, 0, MODE>(p, sQ, sK, bar_item_full, bar_item_empty, slots, &bar_q_full, &bar_q_empty, bar_k_full,
                        bar_k_empty, abort_flag);
     } else if (warp == 1) {
-        producer<D, 1, MODE>(p, sQ, sV, bar_item_full, bar_item_empty, item_slot, &bar_q_full, &bar_q_empty, bar_v_full,
+        producer<D, 1, MODE>(p, sQ, sV, bar_item_full, bar_item_empty, slots, &bar_q_full, &bar_q_empty, bar_v_full,
                        bar_v_empty, abort_flag);
     } else if (warp == 2) {
         if (lane == 0)
-            mma_issuer<D, BF16>(p, tmem, sQ, sK, sV, bar_item_full, bar_item_empty, item_slot, &bar_q_full,
+            mma_issuer<D, BF16>(p, tmem, sQ, sK, sV, bar_item_full, bar_item_empty, slots, &bar_q_full,
                                 &bar_q_empty, bar_k_full, bar_k_empty, bar_v_full, bar_v_empty, bar_s_full, bar_p_full,
-                                &bar_o_done, &bar_o_empty, &bar_drain, abort_flag);
+                                &bar_o_done, &bar_o_empty, &bar_drain, &ctl->final_done, abort_flag);
     } else if (warp >= 4) {
-        softmax_role<D, BF16, MODE>(p, tmem, bar_item_full, bar_item_empty, item_slot, bar_s_full, bar_p_full, &bar_o_done,
+        softmax_role<D, BF16, MODE>(p, tmem, bar_item_full, bar_item_empty, slots, bar_s_full, bar_p_full, &bar_o_done,
                               &bar_o_empty, &bar_wg, &wg_flag, ctl->push_full, ctl->push_empty, ctl->push_item,
-                              abort_flag);
+                              &ctl->final_done, abort_flag);
     } else if (warp == 3 && p.n_out > 1) {
         pusher<D, BF16>(p, ctl->push_full, ctl->push_empty, ctl->push_item, abort_flag);
     }

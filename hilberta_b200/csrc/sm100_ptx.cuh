@@ -280,30 +280,5 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// 2^x for a pair of arguments on the FMA pipe instead of the MUFU pipe (used for
-// a fraction of the softmax exponentials so both pipes share the load).
-// Method: Cody-Waite style range reduction, x = j + f with j = round(x) obtained
-// by adding and subtracting 1.5*2^23 (round-to-nearest), f in [-0.5, 0.5];
-// 2^f by a degree-3 polynomial whose coefficients were fitted for this library
-// (iteratively reweighted least squares on [-0.5, 0.5], max relative error
-// 7.5e-5, far below bf16/fp16 rounding of P); 2^j is added to the exponent
-// field.  Arguments are clamped at -125 so the exponent never wraps (2^-125 is
-// below any probability that survives the 16-bit rounding of P).
-__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& p1) {
-    constexpr float MAGIC = 12582912.0f;  // 1.5 * 2^23
-    const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-    const uint64_t t = f2_add(x, f2_pack(MAGIC, MAGIC));
-    const uint64_t j = f2_add(t, f2_pack(-MAGIC, -MAGIC));
-    const uint64_t f = f2_fma(j, f2_pack(-1.f, -1.f), x);
-    uint64_t p = f2_fma(f, f2_pack(0.05517605f, 0.05517605f), f2_pack(0.24261150f, 0.24261150f));
-    p = f2_fma(p, f, f2_pack(0.69326018f, 0.69326018f));
-    p = f2_fma(p, f, f2_pack(0.99992803f, 0.99992803f));
-    float t0, t1;
-    f2_unpack(t, t0, t1);
-    f2_unpack(p, p0, p1);
-    p0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-    p1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
 }  // namespace ptx
 }  // namespace hb
