@@ -95,6 +95,7 @@ def parse():
     ap.add_argument("--tp-sp", type=int, default=0, choices=(0, 1),
                     help="FLUX step at N > 1: sequence parallelism (token-split streams, all-gather/reduce-scatter)")
     ap.add_argument("--no-4096", action="store_true", help="skip the 4096^2 t16k3 side timing (scaling_4096)")
+    ap.add_argument("--no-sustained", action="store_true", help="skip the sustained 57-call side timing")
     ap.add_argument("--no-triton-reference", action="store_true",
                     help="skip timing the reference's Triton kernel on this GPU (triton_reference)")
     ap.add_argument("--triton-reference-child", action="store_true", help=argparse.SUPPRESS)
@@ -370,7 +371,7 @@ def run_native(a):
 
     # sustained: the 57-call sequence of denoising steps back to back for about
     # half a second, long enough for the 1 kW power cap to act (clocks below)
-    n_sustain = max(4, int(500.0 / (len(DENOISE_PHASES) * weighted_ms)))
+    n_sustain = 0 if a.no_sustained else max(4, int(500.0 / (len(DENOISE_PHASES) * weighted_ms)))
     with torch.inference_mode():
         torch.cuda.synchronize()
         if world > 1:
@@ -388,8 +389,8 @@ def run_native(a):
         s_clocks = merge_clocks(every)
     s_ms = float(s_ms[0])
     s_flop = n_sustain * sum(flops[ph] for ph in DENOISE_PHASES)
-    s_call_ms = s_ms / len(sevs)
-    sustained = {
+    s_call_ms = s_ms / max(1, len(sevs))
+    sustained = None if not sevs else {
         "ms_per_call": round(s_call_ms, 4),
         "value": round(s_flop / (s_ms * 1e-3) / 1e12, 2),
         "steps": n_sustain,
@@ -461,7 +462,7 @@ def run_native(a):
             "workload": workload_name(a.config, H, N),
             "layout": a.layout,
             "heads_per_gpu": hr,
-            "step": "57 calls, the joint attentions of one denoising step (layer i on tile phase i % 4: 15/14/14/14)"
+            "step": "4 calls (tile phases 0-3); ms/call phase-weighted 15/14/14/14"
             + (", each fused with the all-gather of head outputs over NVLink peer memory" if world > 1 else ""),
             "parallelism": f"head-parallel x{world}" if world > 1 else "single GPU",
             "l2": "L2 flushed before every call (a %d MB write outside the per-call events); this GPU's Q+K+V %.0f MB"
@@ -503,12 +504,13 @@ def run_native(a):
             "frac": round(max(t_tensor, t_link) * 1e3 / weighted_ms, 4),
         }
         line["nccl_path"] = nccl
-    sustained["frac_sustained_peak"] = round(sustained["value"] / world / peak_sustained, 4)
-    sustained["peak_sustained"] = peak_sustained
-    sustained["note"] = ("the 57 joint-attention calls of a denoising step (layer i on phase i % 4) back to back, "
-                         "per-call events after an L2 flush; frac against the measured sustained bf16 peak "
-                         "(MEASURED_PEAKS.json bf16_tflops_sustained), the figure for a kernel inside a long step")
-    line["sustained"] = sustained
+    if sustained is not None:
+        sustained["frac_sustained_peak"] = round(sustained["value"] / world / peak_sustained, 4)
+        sustained["peak_sustained"] = peak_sustained
+        sustained["note"] = ("the 57 joint-attention calls of a denoising step (layer i on phase i % 4) back to back, "
+                             "per-call events after an L2 flush; frac against the measured sustained bf16 peak "
+                             "(MEASURED_PEAKS.json bf16_tflops_sustained), the figure for a kernel inside a long step")
+        line["sustained"] = sustained
     line["parity"] = parity
     line["parity_ok"] = parity["ok"]
     if big is not None:
