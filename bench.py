@@ -132,12 +132,37 @@ def ncu_traffic(config):
     return None
 
 
+_SAMPLER = r"""
+import select, sys, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByUUID(sys.argv[1])
+period = float(sys.argv[2])
+get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+    pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+print("ready", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+out = []
+while True:
+    try:
+        out.append((time.time(), pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), get_reasons(h),
+                    pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0))
+    except pynvml.NVMLError:
+        pass
+    if select.select([sys.stdin], [], [], period)[0]:
+        break
+for x in out:
+    print(*x)
+"""
+
+
 class ClockSampler:
     """SM clock, power draw and clock-event reasons of this rank's GPU during the
-    timed region, sampled through NVML (the library behind nvidia-smi's clocks
-    query) every `period` seconds from a thread, so that a region of a few
-    hundred milliseconds still gets tens of samples.  Falls back to
-    ``nvidia-smi -lms 100`` when NVML cannot be opened."""
+    timed region, read through NVML (the library behind nvidia-smi's clocks
+    query) every `period` seconds by a separate process, so the samples keep
+    their pace while this process launches kernels (a thread here would wait
+    for the interpreter lock).  Only samples taken between entering and leaving
+    the block count.  Falls back to ``nvidia-smi -lms 100`` when NVML cannot be
+    opened."""
 
     QUERY = (
         "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -147,72 +172,68 @@ class ClockSampler:
     # NVML clock-event reason bits (nvml.h nvmlClocksEventReason*)
     REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, device, period=0.004):
+    def __init__(self, device, period=0.002):
         self.device, self.period = torch.device(device), period
-        self.samples, self.result, self.proc, self.thread = [], None, None, None
-
-    def _nvml_handle(self):
-        import pynvml
-
-        pynvml.nvmlInit()
-        uuid = "GPU-" + str(torch.cuda.get_device_properties(self.device).uuid)
-        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        self.result, self.proc, self.smi = None, None, None
 
     def __enter__(self):
-        import threading
-
         try:
-            nv, h = self._nvml_handle()
-            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
-            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-                nv.nvmlDeviceGetCurrentClocksThrottleReasons
-        except Exception:  # no NVML: the nvidia-smi query line instead
-            nv = None
-        if nv is not None:
-            self.stop = threading.Event()
-
-            def run():
-                while not self.stop.is_set():
-                    try:
-                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
-                                             int(get_reasons(h)), nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
-                    except Exception:
-                        pass
-                    self.stop.wait(self.period)
-
-            self.thread = threading.Thread(target=run, daemon=True)
-            self.thread.start()
-        else:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.device).uuid)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, uuid, str(self.period)],
+                                         stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            first = self.proc.stdout.readline().split()
+            if not first or first[0] != "ready":
+                raise RuntimeError("NVML sampler did not start")
+            self.max_mhz = float(first[1])
+        except (OSError, RuntimeError, ValueError, IndexError):
+            if self.proc is not None:
+                self.proc.kill()
+                self.proc.wait()
+            self.proc = None
             try:
-                self.proc = subprocess.Popen(
+                self.smi = subprocess.Popen(
                     ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100",
                      "-i", str(self.device.index)],
                     stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             except (OSError, ValueError):
-                self.proc = None
+                self.smi = None
             time.sleep(0.3)
+        self.t0 = time.time()
         return self
 
     def __exit__(self, *exc):
-        if self.thread is not None:
-            self.stop.set()
-            self.thread.join()
-            if self.samples:
-                mhz = [x[0] for x in self.samples]
-                reasons = sorted(n for n, bit in self.REASONS.items() if any(x[1] & bit for x in self.samples))
+        t1 = time.time()
+        if self.proc is not None:
+            try:
+                out, _ = self.proc.communicate(input="stop\n", timeout=30)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            rows = []
+            for line in out.splitlines():
+                f = line.split()
+                if len(f) == 4:
+                    rows.append((float(f[0]), float(f[1]), int(f[2]), float(f[3])))
+            inside = [r for r in rows if self.t0 <= r[0] <= t1]
+            if inside:
+                mhz = [r[1] for r in inside]
+                reasons = sorted(n for n, bit in self.REASONS.items() if any(r[2] & bit for r in inside))
                 self.result = {"sm_mhz": statistics.median(mhz), "sm_min_mhz": min(mhz), "sm_max_mhz": self.max_mhz,
                                "reasons": reasons, "samples": len(mhz),
-                               "power_w_max": round(max(x[2] for x in self.samples), 1), "source": "nvml"}
+                               "power_w_max": round(max(r[3] for r in inside), 1),
+                               "window_ms": round(1e3 * (t1 - self.t0), 1),
+                               "source": "nvml, separate process, every %g ms" % (1e3 * self.period)}
             return False
-        if self.proc is None:
+        if self.smi is None:
             return False
         time.sleep(0.2)
-        self.proc.terminate()
+        self.smi.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            out, _ = self.smi.communicate(timeout=5)
         except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
+            self.smi.kill()
+            out, _ = self.smi.communicate()
         mhz, maxmhz, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.splitlines():
@@ -458,17 +479,9 @@ def run_native(a):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) bf16 Q/K/V, reference benchmark protocol)",
-        "config": {
-            "workload": workload_name(a.config, H, N),
-            "layout": a.layout,
-            "heads_per_gpu": hr,
-            "step": "4 calls (tile phases 0-3); ms/call phase-weighted 15/14/14/14"
-            + (", each fused with the all-gather of head outputs over NVLink peer memory" if world > 1 else ""),
-            "parallelism": f"head-parallel x{world}" if world > 1 else "single GPU",
-            "l2": "L2 flushed before every call (a %d MB write outside the per-call events); this GPU's Q+K+V %.0f MB"
-            % (L2_FLUSH_BYTES >> 20, 3 * N * hr * 128 * 2 / 1e6),
-            "active_blocks_per_phase": active,
-        },
+        "config": shared_config(a.config, H, N, world, a.layout, active),
+        "l2_detail": "this GPU's Q+K+V %.0f MB; the flush is a %d MB write outside the per-call events"
+        % (3 * N * hr * 128 * 2 / 1e6, L2_FLUSH_BYTES >> 20),
         "gpu_launches": len(STEP_PHASES) * a.steps,
         "device_status": status,
         "roofline": {
@@ -1038,6 +1051,21 @@ def workload_name(config, heads, tokens):
     return f"HilbertA paired sparse attention {config}, B=1, H={heads}, D=128, N={tokens}, G=512"
 
 
+def shared_config(config, heads, tokens, world, layout, active):
+    """The ``config`` object both arms print, identical for the same arguments
+    (arm-specific details go in other keys)."""
+    return {
+        "workload": workload_name(config, heads, tokens),
+        "layout": layout,
+        "heads_per_gpu": heads // max(1, world),
+        "step": "4 calls (tile phases 0-3); ms/call phase-weighted 15/14/14/14"
+        + (", each with the all-gather of head outputs" if world > 1 else ""),
+        "parallelism": f"head-parallel x{world}" if world > 1 else "single GPU",
+        "l2": "GPU arm: L2 flushed before every call; CPU arm: no device cache involved",
+        "active_blocks_per_phase": list(active),
+    }
+
+
 class CpuDenseMask:
     """The reference's dense-mask CPU path (plan mask + fp32 SDPA, the
     computation of hilberta/plan.py:70-84 with flux_adapter.py:299-307), as
@@ -1150,12 +1178,10 @@ def run_reference(a):
         "vs_baseline": None,
         "dtype": "f32 (from bf16 inputs)",
         "data": "synthetic (seeded N(0,1) bf16 Q/K/V, reference benchmark protocol)",
-        "config": {
-            "workload": workload_name(a.config, a.heads, N),
-            "path": "reference dense-mask CPU path (plan.dense_mask + fp32 SDPA), oracle port",
-            "step_sample": sample,
-            "plan": "oracle/plan_oracle.py bridge_k_plan (restatement of hilberta/bridge_k.py, pinned by goldens)",
-        },
+        "config": shared_config(a.config, a.heads, N, a.gpus, a.layout, active),
+        "path": "reference dense-mask CPU path (plan.dense_mask + fp32 SDPA), oracle port",
+        "step_sample": sample,
+        "plan": "oracle/plan_oracle.py bridge_k_plan (restatement of hilberta/bridge_k.py, pinned by goldens)",
         "extrapolated": {
             "ms_per_call": round(weighted_call_flop / (value * 1e12) * 1e3, 1),
             "ms_per_step": round(full_step_flop / (value * 1e12) * 1e3, 1),

@@ -36,6 +36,9 @@ def test_reference_arm_prints_contract_line():
     import bench
 
     assert line["config"]["workload"] == bench.workload_name("1024_t4k1", 24, 4608)
+    # the whole config object is the one the native arm prints for the same arguments
+    active = line["config"]["active_blocks_per_phase"]
+    assert line["config"] == bench.shared_config("1024_t4k1", 24, 4608, 1, "bhnd", active)
     assert line["ms_per_step"] < 5000  # measured wall time of one bounded sample, not an extrapolation
     assert line["extrapolated"]["ms_per_call"] > 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
