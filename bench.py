@@ -349,10 +349,13 @@ def run_native(a):
     with torch.inference_mode():
         run_steps(max(3, a.warmup), False)
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # the sampler process starts first (its start-up time differs between
+        # ranks), then the barrier lines the ranks up: a fused call waits for
+        # every rank's rows, so a rank that starts late would inflate the first call
         with ClockSampler(dev, period=0.002) as clk:
+            if world > 1:
+                dist.barrier()
             torch.cuda.synchronize()
             t0.record(stream)
             evs = run_steps(a.steps, True)
@@ -395,9 +398,10 @@ def run_native(a):
     n_sustain = 0 if a.no_sustained else max(4, int(500.0 / (len(DENOISE_PHASES) * weighted_ms)))
     with torch.inference_mode():
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
         with ClockSampler(dev, period=0.01) as clk_s:
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
             sevs = run_steps(n_sustain, True, DENOISE_PHASES)
             torch.cuda.synchronize()
         status |= hb.device_status(dev)

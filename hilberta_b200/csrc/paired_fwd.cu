@@ -538,46 +538,57 @@ __device__ void mma_issuer(const FwdParams& p, uint32_t tmem, uint8_t* sQ, uint8
     }
 }
 
+// Copy of `nrows` finished output rows (from row `row0` of head offset `hb_off`)
+// from this rank's output, read back from L2, to every other rank's output with
+// lane-consecutive 16-byte stores (whole rows per warp instruction: the pattern
+// that keeps NVLink writes in full lines).  One warp; nrows a multiple of the
+// rows one instruction covers.
+template <int D, bool BF16>
+__device__ __forceinline__ void push_rows(const FwdParams& p, int64_t hb_off, int row0, int nrows) {
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    constexpr int CPR = D / 8;     // 16-byte chunks per row
+    constexpr int RPI = 32 / CPR;  // rows per warp instruction
+    constexpr int BATCH = 8;
+    const int lane = threadIdx.x & 31;
+    const T* src = reinterpret_cast<const T*>(p.outs[p.rank]);
+    const int r0 = row0 + lane / CPR;
+    const int ni = nrows / RPI;  // instructions per destination
+    // loads in batches ahead of their stores: the destinations could alias the
+    // source as far as the compiler knows
+#pragma unroll 1
+    for (int i0 = 0; i0 < ni; i0 += BATCH) {
+        uint4 v4[BATCH];
+#pragma unroll
+        for (int i = 0; i < BATCH; i++)
+            if (i0 + i < ni)
+                v4[i] = __ldcg(reinterpret_cast<const uint4*>(src + hb_off + (int64_t)(r0 + (i0 + i) * RPI) * p.o_sn) +
+                               lane % CPR);
+        for (int d = 0; d < p.n_out; d++) {
+            if (d == p.rank) continue;
+            T* dst = reinterpret_cast<T*>(p.outs[d]) + hb_off;
+#pragma unroll
+            for (int i = 0; i < BATCH; i++)
+                if (i0 + i < ni)
+                    *(reinterpret_cast<uint4*>(dst + (int64_t)(r0 + (i0 + i) * RPI) * p.o_sn) + lane % CPR) = v4[i];
+        }
+    }
+}
+
 // Fused all-gather, run by warp 3 while the softmax warps go on with the next
-// item: each finished item's 128 output rows, already in this rank's output, are
-// read back from L2 and stored to every other rank with lane-consecutive 16-byte
-// stores (whole rows per instruction).  Items arrive through a two-slot ring;
-// item -1 ends the loop.
+// item: each finished item's 128 output rows, already in this rank's output, go
+// to every other rank (push_rows).  Items arrive through a two-slot ring; item
+// -1 ends the loop.
 template <int D, bool BF16>
 __device__ void pusher(const FwdParams& p, uint64_t* bar_full, uint64_t* bar_empty, const int* push_item,
                        volatile int* abort_flag) {
-    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    constexpr int CPR = D / 8;          // 16-byte chunks per row
-    constexpr int RPI = 32 / CPR;       // rows per warp instruction
-    constexpr int NI = 128 / RPI;       // instructions per destination for the item's 128 rows
-    constexpr int BATCH = NI < 8 ? NI : 8;
     const int lane = threadIdx.x & 31;
-    const T* src = reinterpret_cast<const T*>(p.outs[p.rank]);
     for (uint32_t k = 0;; k++) {
         const int ps = k & 1;
         if (!warp_wait(&bar_full[ps], (k >> 1) & 1, abort_flag, p.timeout)) return;
         const int item = push_item[ps];
         if (item < 0) return;
         const Item w = decode_item_n(p, item, 0);  // rows only
-        const int64_t hb_off = (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh;
-        const int row0 = w.qrow0 + lane / CPR;
-        // loads in batches ahead of their stores: the destinations could alias the
-        // source as far as the compiler knows
-#pragma unroll 1
-        for (int i0 = 0; i0 < NI; i0 += BATCH) {
-            uint4 v4[BATCH];
-#pragma unroll
-            for (int i = 0; i < BATCH; i++)
-                v4[i] = __ldcg(reinterpret_cast<const uint4*>(src + hb_off + (int64_t)(row0 + (i0 + i) * RPI) * p.o_sn) +
-                               lane % CPR);
-            for (int d = 0; d < p.n_out; d++) {
-                if (d == p.rank) continue;
-                T* dst = reinterpret_cast<T*>(p.outs[d]) + hb_off;
-#pragma unroll
-                for (int i = 0; i < BATCH; i++)
-                    *(reinterpret_cast<uint4*>(dst + (int64_t)(row0 + (i0 + i) * RPI) * p.o_sn) + lane % CPR) = v4[i];
-            }
-        }
+        push_rows<D, BF16>(p, (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh, w.qrow0, 128);
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_empty[ps]);
     }
@@ -635,7 +646,19 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
     // was ready, and MMAs complete in issue order; on the way out it is waited
     // for explicitly) and the next PV needs this epilogue's o_empty first.  O's
     // TMEM is free for the next item's first PV once it returns.
-    auto finish = [&](const Pending& pd) -> bool {
+    // Fused all-gather: a finished item's rows (in this rank's output) go to the
+    // other ranks.  Items are handed to warp 3, which copies them while these
+    // warps compute the next item; the CTA's final item, with nothing left to
+    // compute, is copied by the four softmax warps themselves (each its own 32
+    // rows), so the launch's tail is not one warp's copy of a whole item.
+    auto hand_over = [&](int item, const Item& w, bool last) -> bool {
+        if (!last) return enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, item, abort_flag);
+        __threadfence();
+        __syncwarp();
+        push_rows<D, BF16>(p, (int64_t)w.b * p.o_sb + (int64_t)w.h * p.o_sh, w.qrow0 + (r & ~31), 32);
+        return true;
+    };
+    auto finish = [&](const Pending& pd, bool last) -> bool {
         const Item w = decode_item_n(p, pd.item, pd.n);
         if (!warp_wait(bar_o_done, pd.last_pv & 1, abort_flag, p.timeout)) return false;
         tc_fence_after();
@@ -694,8 +717,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_o_empty);
-            if (push && !enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, pd.item, abort_flag))
-                return false;
+            if (push && !hand_over(pd.item, w, last)) return false;
         } else {
             constexpr int PSTRIDE = 128 * D + 256;
             float* rec = p.partial + ((int64_t)w.group * p.n_chunks + w.chunk) * PSTRIDE;
@@ -733,29 +755,31 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             if (*wg_flag) {
                 __threadfence();
                 const float* base = p.partial + (int64_t)w.group * p.n_chunks * PSTRIDE;
-                float wt[MAX_CHUNKS];
+                // chunk weights 2^(m_c - max) are recomputed where used (no
+                // indexed local array, which would live in local memory)
                 float mmax = -INFINITY;
                 for (int c = 0; c < p.n_chunks; c++) mmax = fmaxf(mmax, __ldcg(base + c * PSTRIDE + 128 * D + r));
-                float lsum = 0.f;
-                for (int c = 0; c < p.n_chunks; c++) {
+                auto weight = [&](int c) {
                     const float mc = __ldcg(base + c * PSTRIDE + 128 * D + r);
-                    wt[c] = mc == -INFINITY ? 0.f : ex2(mc - mmax);
-                    lsum += wt[c] * __ldcg(base + c * PSTRIDE + 128 * D + 128 + r);
-                }
+                    return mc == -INFINITY ? 0.f : ex2(mc - mmax);
+                };
+                float lsum = 0.f;
+                for (int c = 0; c < p.n_chunks; c++) lsum += weight(c) * __ldcg(base + c * PSTRIDE + 128 * D + 128 + r);
                 const float inv = 1.f / lsum;
                 for (int c = 0; c < D / 32; c++) {
                     float vals[32];
 #pragma unroll
                     for (int i = 0; i < 32; i++) vals[i] = 0.f;
                     for (int k = 0; k < p.n_chunks; k++) {
+                        const float wk = weight(k);
                         const float4* src = reinterpret_cast<const float4*>(base + k * PSTRIDE + r * D + 32 * c);
 #pragma unroll
                         for (int i = 0; i < 8; i++) {
                             const float4 v4 = __ldcg(src + i);
-                            vals[4 * i] += wt[k] * v4.x;
-                            vals[4 * i + 1] += wt[k] * v4.y;
-                            vals[4 * i + 2] += wt[k] * v4.z;
-                            vals[4 * i + 3] += wt[k] * v4.w;
+                            vals[4 * i] += wk * v4.x;
+                            vals[4 * i + 1] += wk * v4.y;
+                            vals[4 * i + 2] += wk * v4.z;
+                            vals[4 * i + 3] += wk * v4.w;
                         }
                     }
                     uint32_t packed[16];
@@ -763,8 +787,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                     for (int i = 0; i < 16; i++) packed[i] = pack2<BF16>(vals[2 * i] * inv, vals[2 * i + 1] * inv);
                     store32(32 * c, packed);
                 }
-                if (push && !enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, pd.item, abort_flag))
-                    return false;
+                if (push && !hand_over(pd.item, w, last)) return false;
             }
         }
         return true;
@@ -786,7 +809,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             // completed (the issuer's final commit), then finish() finds the
             // last PV's o_done phase complete and no later one.
             if (pending && !warp_wait(bar_final, 0, abort_flag, p.timeout)) return;
-            if (pending && !finish(pend)) return;
+            if (pending && !finish(pend, true)) return;
             if (p.n_out > 1) enqueue_push(p, bar_push_full, bar_push_empty, push_item, npush, -1, abort_flag);
             return;
         }
@@ -887,7 +910,7 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
         // first PV, which needs O's TMEM, follows right after), then the rest
         if (!step(0)) return;
         if (pending) {
-            if (!finish(pend)) return;
+            if (!finish(pend, false)) return;
             pending = false;
         }
         for (int j = 1; j < w.n; j++)

@@ -73,6 +73,32 @@ def test_loopback_writes_every_destination_and_flags():
     assert _lib.HB_DEV_PEER_TIMEOUT == 8
 
 
+def test_loopback_more_items_than_ctas_matches_oracle():
+    """24 heads at grid 64 give more work items than CTAs: items finished mid-launch
+    go through warp 3's copy ring, each CTA's last item through the softmax warps'
+    own copy; both destinations must equal the local kernel bit for bit, and
+    sampled rows the fp32 oracle."""
+    import hilberta_b200 as hb
+
+    meta, q, k, v = _setup(heads=24, grid=64, seed=5, phase=2)
+    with torch.inference_mode():
+        ref = hb.paired_attention(q, k, v, meta)
+    outs = [torch.full_like(q, float("nan")) for _ in range(2)]
+    flags = [torch.zeros(8, dtype=torch.int32, device="cuda") for _ in range(2)]
+    flags[0][1] = 1
+    _loopback(q, k, v, meta, outs, flags, 1, 2000)
+    assert hb.device_status() == 0
+    assert torch.equal(outs[0], ref) and torch.equal(outs[1], ref)
+    plan = hb.bridge_k_plan(4, 1, False, grid_size=64)
+    p = plan.phases[2]
+    N, G = plan.total_tokens, plan.global_tokens
+    rows = torch.tensor([0, G - 1, G, G + 63, G + 64, N // 2, N - 1])
+    mask = ao.block_mask_from_rows(p.kv_indices, p.kv_counts, N, G)
+    want = ao.masked_attention_fp32(q.cpu(), k.cpu(), v.cpu(), mask, rows=rows)
+    err = (outs[1].cpu()[:, :, rows].float() - want).abs()
+    assert float(err.max()) <= 2e-2 and float(err.mean()) <= 2e-3
+
+
 def test_missing_peer_times_out_and_context_survives():
     import hilberta_b200 as hb
     from hilberta_b200 import _lib
@@ -111,7 +137,7 @@ def _rank(rank, world, port, result):
         metas = [
             hb.pair_metadata(p.kv_indices, p.kv_counts, tokens=N, global_tokens=G).to(dev) for p in plan.phases
         ]
-        H = 8
+        H = 24  # 12 heads per rank: more work items than CTAs, so both copy paths run
         full = [x.to(dev) for x in ao.seeded_qkv(1, H, N, 128, seed=21)]
         ok = True
         for layout in ("bhnd", "bnhd"):
