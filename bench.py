@@ -435,11 +435,12 @@ def run_native(a):
                          device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         parity.update(max_abs=float(t[0]), mean_abs=float(t[1]), ok=not bool(t[2]), ranks_checked=world)
-    link_gbs = None
+    link_gbs = link_ce_gbs = None
     if world > 1:
-        link_gbs = torch.tensor([fused.measure_link_gbs()], dtype=torch.float64, device=dev)
-        dist.all_reduce(link_gbs, op=dist.ReduceOp.MIN)
-        link_gbs = float(link_gbs[0])
+        t = torch.tensor([fused.measure_link_gbs(method="sm"), fused.measure_link_gbs(method="copy_engine")],
+                         dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        link_gbs, link_ce_gbs = float(t[0]), float(t[1])
     perm = permutation_side_timing(a, q, k, v, metas, plan, dev, hb) if world == 1 else None
     prep_t = prep_side_timing(plan, H, dev) if world == 1 else None
     flux = None if a.no_flux_step else flux_step_timing(a, dev, world)
@@ -508,14 +509,16 @@ def run_native(a):
     if world > 1:
         # fused compute + collective: the target is the slower of the tensor time
         # and this GPU's share of the NVLink traffic (its rows to P-1 peers)
-        link = link_gbs  # GB/s this rank sends, plain peer copies measured in this run (slowest rank)
+        link = link_gbs  # GB/s this rank sends with SM stores, measured in this run (slowest rank)
         nv_bytes = (world - 1) * N * hr * 128 * 2
         t_tensor = weighted_flop / world / (peak * 1e12)
         t_link = nv_bytes / (link * 1e9)
         line["roofline"]["fused_allgather"] = {
             "nvlink_bytes_per_call": nv_bytes,
             "link_gbs": round(link, 1),
-            "link_source": "measured now: hb_peer_copy of each rank's rows to every peer, all ranks at once, best of 3",
+            "link_source": "measured now: hb_peer_scatter (SM stores in the fused kernel's pattern) of each rank's "
+            "rows to every peer, all ranks at once, best of 3, slowest rank",
+            "link_gbs_copy_engine": round(link_ce_gbs, 1),
             "target_ms": round(max(t_tensor, t_link) * 1e3, 4),
             "bound": "tensor" if t_tensor >= t_link else "nvlink",
             "frac": round(max(t_tensor, t_link) * 1e3 / weighted_ms, 4),

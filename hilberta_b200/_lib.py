@@ -57,6 +57,7 @@ EXPORTS = (
     "hb_ipc_open",
     "hb_ipc_close",
     "hb_peer_copy",
+    "hb_peer_scatter",
     "hb_adaln_residual",
     "hb_expand_kv128",
 )
@@ -132,6 +133,7 @@ _SIGS = {
     "hb_ipc_open": (_I, [_P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
     "hb_ipc_close": (_I, [_P, ctypes.c_uint64]),
     "hb_peer_copy": (_I, [_P, _P, ctypes.c_size_t, _P]),
+    "hb_peer_scatter": (_I, [_P, ctypes.POINTER(ctypes.c_void_p), _I, ctypes.c_size_t, _P]),
     "hb_expand_kv128": (_I, [_P, _P, _I64, _I, _P, _I, _P, _P, _I64, _P, _P]),
     "hb_adaln_residual": (
         _I,

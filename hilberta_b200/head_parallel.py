@@ -168,39 +168,47 @@ class PeerAllGather:
         _launch_allgather(q, k, v, full, metadata, N_, G, scale, peers)
         return full
 
-    def measure_link_gbs(self, reps=3):
-        """Collective, between calls only: every rank copies the bytes one call
-        sends to each peer (its own head rows) into every peer's buffer with
-        plain copy-engine transfers (``hb_peer_copy``, one stream per peer), all
-        ranks at once, as the fused call's stores load the links.  Returns this
-        rank's send bandwidth in GB/s (bytes sent over device time, best of
-        `reps`).  It overwrites the buffers' contents."""
+    def measure_link_gbs(self, reps=3, method="sm"):
+        """Collective, between calls only: every rank sends the bytes one call
+        sends to each peer (its own head rows) into every peer's buffer, all
+        ranks at once, as the fused call's stores load the links.  ``method``
+        "sm": one ``hb_peer_scatter`` launch, SM stores to all peers in the fused
+        kernel's pattern; "copy_engine": plain copy-engine transfers
+        (``hb_peer_copy``, one stream per peer).  Returns this rank's send
+        bandwidth in GB/s (bytes sent over device time, best of `reps`).  It
+        overwrites the buffers' contents."""
         if self._ptrs is None:
             raise RuntimeError("PeerAllGather is closed")
+        if method not in ("sm", "copy_engine"):
+            raise ValueError("method must be 'sm' or 'copy_engine'")
         B, H, N, D = self.shape
         nbytes = B * (self.head1 - self.head0) * N * D * self._bufs[0].element_size()
         src = self._ptrs[self.rank][1] + self.rank * nbytes  # this rank's region of its idle second buffer
         lib = _lib.lib()
         main = torch.cuda.current_stream(self.device)
-        side = [torch.cuda.Stream(self.device) for _ in range(self.world - 1)]
+        peers = [r for r in range(self.world) if r != self.rank]
+        side = [torch.cuda.Stream(self.device) for _ in peers] if method == "copy_engine" else []
+        dsts = (ctypes.c_void_p * len(peers))(*[self._ptrs[r][0] + self.rank * nbytes for r in peers])
         best = float("inf")
         for _ in range(reps):
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(main)
-            peers = [r for r in range(self.world) if r != self.rank]
-            for s, r in zip(side, peers):
-                s.wait_event(e0)
-                _lib.check(lib.hb_peer_copy(ctypes.c_void_p(self._ptrs[r][0] + self.rank * nbytes),
-                                            ctypes.c_void_p(src), nbytes, ctypes.c_void_p(s.cuda_stream)),
-                           "hb_peer_copy")
-                main.wait_stream(s)
+            if method == "sm":
+                _lib.check(lib.hb_peer_scatter(ctypes.c_void_p(src), dsts, len(peers), nbytes,
+                                               ctypes.c_void_p(main.cuda_stream)), "hb_peer_scatter")
+            else:
+                for s, d in zip(side, dsts):
+                    s.wait_event(e0)
+                    _lib.check(lib.hb_peer_copy(ctypes.c_void_p(d), ctypes.c_void_p(src), nbytes,
+                                                ctypes.c_void_p(s.cuda_stream)), "hb_peer_copy")
+                    main.wait_stream(s)
             e1.record(main)
             torch.cuda.synchronize(self.device)
             best = min(best, e0.elapsed_time(e1))
         dist.barrier(group=self.group)
-        return (self.world - 1) * nbytes / (best * 1e-3) / 1e9
+        return len(peers) * nbytes / (best * 1e-3) / 1e9
 
     def close(self):
         """Unmap the peers' buffers once every rank is done with every call (collective)."""

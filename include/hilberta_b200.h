@@ -249,6 +249,14 @@ int hb_ipc_close(void* ptr, uint64_t offset);
  * that callers time to know the NVLink bandwidth the fused all-gather's peer
  * stores are held against. */
 int hb_peer_copy(void* dst, const void* src, size_t bytes, void* stream);
+/* `bytes` from `src` to each of the n_dst destinations (1..HB_MAX_RANKS; any of
+ * them may be hb_ipc_open mappings) by SM stores: two CTAs per SM, each lane
+ * loading 16 bytes and storing them to every destination, consecutive lanes on
+ * consecutive 16-byte chunks (the store pattern of the fused all-gather's peer
+ * copies).  Pointers 16-byte aligned, bytes a multiple of 16.  No counterpart
+ * in the reference: callers time it to know the NVLink bandwidth those stores
+ * reach when every rank sends at once. */
+int hb_peer_scatter(const void* src, void* const* dst, int n_dst, size_t bytes, void* stream);
 
 /* ---- Q/K/V preparation before the attention ----------------------------- */
 /* The FLUX processor's steps between the projections and the attention

@@ -108,6 +108,14 @@ def test_allgather_argument_checks(lib):
     off = ctypes.c_uint64()
     assert lib.hb_ipc_export(None, handle, ctypes.byref(off)) == _lib.HB_ERR_ARG
     assert lib.hb_ipc_open(None, 0, ctypes.byref(ctypes.c_void_p())) == _lib.HB_ERR_ARG
+    # the SM-store scatter: destination count, 16-byte alignment and size are checked first
+    fake = ctypes.c_void_p(1 << 20)
+    dsts = (ctypes.c_void_p * 2)(1 << 21, 1 << 22)
+    assert lib.hb_peer_scatter(fake, dsts, 0, 64, None) == _lib.HB_ERR_ARG
+    assert lib.hb_peer_scatter(fake, dsts, _lib.HB_MAX_RANKS + 1, 64, None) == _lib.HB_ERR_ARG
+    assert lib.hb_peer_scatter(fake, dsts, 2, 40, None) == _lib.HB_ERR_ARG
+    assert lib.hb_peer_scatter(ctypes.c_void_p((1 << 20) + 8), dsts, 2, 64, None) == _lib.HB_ERR_ARG
+    assert lib.hb_peer_scatter(None, dsts, 2, 64, None) == _lib.HB_ERR_ARG
     assert lib.hb_ipc_close(None, 0) == _lib.HB_ERR_ARG
 
 

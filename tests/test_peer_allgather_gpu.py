@@ -99,6 +99,25 @@ def test_loopback_more_items_than_ctas_matches_oracle():
     assert float(err.max()) <= 2e-2 and float(err.mean()) <= 2e-3
 
 
+def test_peer_scatter_copies_to_every_destination():
+    """hb_peer_scatter (the link measurement's SM-store copy) on local buffers:
+    every destination equals the source, bytes outside the range untouched."""
+    import ctypes
+
+    from hilberta_b200 import _lib
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    src = torch.randint(-(2**31), 2**31 - 1, (3 << 18,), generator=g, dtype=torch.int32, device="cuda")
+    dst = [torch.zeros(src.numel() + 64, dtype=torch.int32, device="cuda") for _ in range(3)]
+    ptrs = (ctypes.c_void_p * 3)(*[d.data_ptr() for d in dst])
+    rc = _lib.lib().hb_peer_scatter(ctypes.c_void_p(src.data_ptr()), ptrs, 3, src.numel() * 4,
+                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == _lib.HB_OK
+    torch.cuda.synchronize()
+    for d in dst:
+        assert torch.equal(d[: src.numel()], src) and not d[src.numel():].any()
+
+
 def test_missing_peer_times_out_and_context_survives():
     import hilberta_b200 as hb
     from hilberta_b200 import _lib
