@@ -11,9 +11,10 @@ per-token cos/sin read from a cache indexed by position), so the restatement
 and ``hb_norm_rope_pack``'s rotation are checked against it here, with FLUX's
 3-axis angles.  flashinfer rounds a fused multiply-add where the restatement
 (like diffusers' torch ops) rounds each product, so a 16-bit result may differ
-by one unit in the last place; the test bounds that at one ulp on a small
-fraction of elements.  The normalisation step is checked against torch's own
-``rms_norm`` on the CPU (test_processor.py covers the rest).
+in its last place, and by a few fp32 rounding errors where the pair's two
+products cancel; the test allows exactly that, on a small fraction of
+elements.  The normalisation step is checked against torch's own ``rms_norm``
+on the CPU (test_processor.py).
 """
 
 from __future__ import annotations
@@ -54,9 +55,16 @@ def _flashinfer_rope(x, cos_half, sin_half):
     return out.reshape(B, S, H, D).cpu()
 
 
-def _ulps(a, b):
-    ia, ib = a.view(torch.int16).to(torch.int32), b.view(torch.int16).to(torch.int32)
-    return (ia - ib).abs()
+def _check_close(got, want, x):
+    """got equals want but for rounding: each element within one 16-bit step of
+    want, or, where the pair's two products cancel, within a few fp32 rounding
+    errors of their magnitudes; differing elements rare.  A wrong pairing, sign
+    or angle gives errors of the order of the values themselves."""
+    eps = torch.finfo(x.dtype).eps
+    mag = x.float().reshape(*x.shape[:-1], -1, 2).abs().sum(-1).repeat_interleave(2, dim=-1)
+    diff = (got.float() - want.float()).abs()
+    assert bool((diff <= eps * want.float().abs() + 2.0**-18 * mag).all()), float(diff.max())
+    assert float((got != want).float().mean()) < 0.02
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -69,13 +77,11 @@ def test_rotation_matches_flashinfer_interleaved_rope(dtype):
     cos, sin = cos_half.repeat_interleave(2, dim=1), sin_half.repeat_interleave(2, dim=1)
     want = _flashinfer_rope(x, cos_half, sin_half)
     # the CPU restatement (diffusers' op order)
-    d = _ulps(po.apply_rope(x, cos, sin), want)
-    assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 0.02
+    _check_close(po.apply_rope(x, cos, sin), want, x)
     # the kernel's rotation (no normalisation weights: rotation and packing only)
     from hilberta_b200 import prep
 
     dev = torch.device("cuda", 0)
     with torch.inference_mode():
         got = prep.norm_rope_pack(None, x.flatten(2).to(dev), heads=H, cos=cos.to(dev), sin=sin.to(dev)).cpu()
-    d = _ulps(got, want)
-    assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 0.02
+    _check_close(got, want, x)
