@@ -526,6 +526,9 @@ def run_native(a):
             "frac": round(max(t_tensor, t_link) * 1e3 / weighted_ms, 4),
         }
         line["nccl_path"] = nccl
+        # the north star asks for kernel-only and kernel + gather separately at N > 1
+        line["kernel_only"] = {"ms_per_call": nccl["kernel_ms_per_call"], "value": nccl["kernel_only_value"],
+                               "unit": "TFLOP/s", "note": "attention launches without the all-gather (nccl_path)"}
     if sustained is not None:
         sustained["frac_sustained_peak"] = round(sustained["value"] / world / peak_sustained, 4)
         sustained["peak_sustained"] = peak_sustained
@@ -839,7 +842,9 @@ def nccl_side_timing(a, q, k, v, metas, flops, world, dev, hb, steps=5):
         "ms_per_step": round(float(t[0]), 4),
         "kernel_ms_per_call": round(float(t[1]), 4),
         "value": round(sum(flops) / (float(t[0]) * 1e-3) / 1e12, 2),
-        "note": "paired_attention into a local output, then dist.all_gather_into_tensor (NCCL), per call",
+        "kernel_only_value": round(sum(flops) / len(flops) / (float(t[1]) * 1e-3) / 1e12, 2),
+        "note": "paired_attention into a local output, then dist.all_gather_into_tensor (NCCL), per call; "
+        "kernel_only_value: whole-job TFLOP/s of the attention launches alone (this rank's heads, max over ranks)",
     }
 
 
