@@ -719,17 +719,20 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
             if (lane == 0) mbar_arrive(bar_o_empty);
             if (push && !hand_over(pd.item, w, last)) return false;
         } else {
+            // a chunk's record: O as float4 groups of 4 columns, group-major
+            // ([D/4][128 rows][4]), so the 32 rows of a warp fill 512 contiguous bytes
+            // per store (and per load in the merge); then m [128] and l [128]
             constexpr int PSTRIDE = 128 * D + 256;
             float* rec = p.partial + ((int64_t)w.group * p.n_chunks + w.chunk) * PSTRIDE;
+            float4* rec4 = reinterpret_cast<float4*>(rec);
 #pragma unroll
             for (int c = 0; c < D / 32; c++) {
                 uint32_t o[32];
                 tmem_ld32(t_lane + C::O_COL + 32 * c, o);
-                float4* dst = reinterpret_cast<float4*>(rec + r * D + 32 * c);
 #pragma unroll
                 for (int i = 0; i < 8; i++)
-                    dst[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
-                                         __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+                    rec4[(8 * c + i) * 128 + r] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                                              __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
             }
             rec[128 * D + r] = pd.m;
             rec[128 * D + 128 + r] = pd.l;
@@ -772,10 +775,10 @@ __device__ void softmax_role(const FwdParams& p, uint32_t tmem, uint64_t* bar_it
                     for (int i = 0; i < 32; i++) vals[i] = 0.f;
                     for (int k = 0; k < p.n_chunks; k++) {
                         const float wk = weight(k);
-                        const float4* src = reinterpret_cast<const float4*>(base + k * PSTRIDE + r * D + 32 * c);
+                        const float4* src = reinterpret_cast<const float4*>(base + k * PSTRIDE);
 #pragma unroll
                         for (int i = 0; i < 8; i++) {
-                            const float4 v4 = __ldcg(src + i);
+                            const float4 v4 = __ldcg(src + (8 * c + i) * 128 + r);
                             vals[4 * i] += wk * v4.x;
                             vals[4 * i + 1] += wk * v4.y;
                             vals[4 * i + 2] += wk * v4.z;
