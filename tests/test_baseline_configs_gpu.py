@@ -13,6 +13,8 @@ mean-abs <= 2e-3, on the full 24 heads of the BASELINE shapes:
   16-tile K3 (the headline shape): every phase, >= 256 sampled rows per phase
   (global rows including the first and last, both halves of 64+ pair-rows, the
   last row);
+* 4096^2 16-tile K3 (performance only in BASELINE): phases 0 and 3, sampled rows,
+  physical order;
 
 each in the physical token order of the metadata and in raster token order
 (8x8-square TMA boxes, ``token_order=raster_order(plan)``), where the inputs
@@ -99,3 +101,27 @@ def test_2048_t16k3_all_phases_sampled_rows():
 
 def test_1024_t16k3_all_phases_all_rows():
     _config(16, 3, 64, all_rows=True, seed=2710)
+
+
+def test_4096_t16k3_sampled_rows_phases_0_and_3():
+    """The performance-only BASELINE shape (66 048 tokens, 24 heads), physical
+    order, phases 0 and 3: the widest rows (75 paired entries), where each
+    global row's last key blocks run as separate tail chunks merged at the end."""
+    import hilberta_b200 as hb
+
+    dev = torch.device("cuda", 0)
+    plan = hb.bridge_k_plan(16, 3, False, grid_size=256)
+    N, G = plan.total_tokens, plan.global_tokens
+    q, kk, v = ao.seeded_qkv(1, 24, N, 128, seed=2711)
+    dq, dk, dv = (x.to(dev) for x in (q, kk, v))
+    for phase in (0, 3):
+        p = plan.phases[phase]
+        meta = hb.pair_metadata(p.kv_indices, p.kv_counts, tokens=N, global_tokens=G).to(dev)
+        with torch.inference_mode():
+            got = hb.paired_attention(dq, dk, dv, meta, **KW)
+        torch.cuda.synchronize()
+        assert hb.device_status() == 0
+        rows = _sample_rows(N, G, 2711 + phase)
+        want = ao.masked_attention_fp32(q, kk, v, ao.block_mask_from_rows(p.kv_indices, p.kv_counts, N, G),
+                                        rows=rows)
+        _check(got[:, :, torch.from_numpy(rows).to(dev)].cpu(), want, f"4096^2 physical order, phase {phase}")
